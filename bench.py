@@ -1,0 +1,436 @@
+"""Benchmark: Qwen3-8B bf16 continuous-batching decode step through the nvkv
+hot path, tensor-parallel over N GPUs (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nvkv|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (Qwen3-8B shapes, random-init weights): 256
+running sequences whose 1024-token prompts are already prefilled and which are
+mid-generation, so their contexts are drawn (seeded) uniform in [1025, 1536];
+one step decodes one token for every sequence through all 36 layers:
+embedding -> 36 x [RMSNorm, qkv GEMM, nvkv_qknorm_rope (+KV store),
+nvkv_paged_attention (split-KV decode), o_proj GEMM (+all-reduce), RMSNorm,
+gate_up GEMM, SiLU*mul, down GEMM (+all-reduce)] -> norm -> lm_head
+(+all-gather) -> argmax.  The per-step KV read (~48 GB at TP1) is far larger
+than L2, so no flush is needed between steps.
+
+One JSON line is printed by rank 0 (see the keys in main()).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nanovllm-rs_b200"))
+
+METRIC = "decode tok/s Qwen3-8B bf16 at TP1/2/4/8; paged-attn HBM GB/s vs 8 TB/s"
+NUM_SEQS = 256
+PROMPT = 1024
+MAX_OUT = 512
+PAGE = 256
+SEED = 1234
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="nvkv", choices=["nvkv", "reference"])
+    ap.add_argument("--no-graph", action="store_true", help="eager launches (no CUDA graph)")
+    ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
+    return ap.parse_args()
+
+
+def workload(seed=SEED):
+    """Seeded decode-step metadata, built like ModelRunner::prepare_model_input
+    (model_runner.rs:82-131) for 256 sequences each decoding one token."""
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(PROMPT + 1, PROMPT + MAX_OUT + 1, NUM_SEQS)  # context incl. new token
+    nblk = (ctx + PAGE - 1) // PAGE
+    num_blocks = int(nblk.sum()) + 8
+    perm = rng.permutation(num_blocks)
+    width = int(nblk.max())
+    bt = np.zeros((NUM_SEQS, width), np.int32)
+    used = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[used:used + n]
+        used += n
+    pos = ctx - 1
+    slots = bt[np.arange(NUM_SEQS), pos // PAGE].astype(np.int64) * PAGE + pos % PAGE
+    return dict(ctx=ctx, block_tables=bt, num_blocks=num_blocks, positions=pos.astype(np.int64),
+                slot_mapping=slots, input_ids=rng.integers(0, 151936, NUM_SEQS).astype(np.int64),
+                cu_q=np.arange(NUM_SEQS + 1, dtype=np.int32),
+                cu_k=np.concatenate([[0], np.cumsum(ctx)]).astype(np.int32),
+                max_k=int(ctx.max()))
+
+
+def decode_bytes(w, hq, hkv, D=128):
+    """Algorithmic HBM bytes of one decode-attention launch (one layer):
+    K+V rows of every context, q and out rows, block-table entries, cu_seqlens."""
+    kv = int(w["ctx"].sum()) * hkv * D * 2 * 2
+    qo = 2 * NUM_SEQS * hq * D * 2
+    meta = 4 * int(((w["ctx"] + PAGE - 1) // PAGE).sum()) + 2 * 4 * (NUM_SEQS + 1)
+    return kv + qo + meta
+
+
+def load_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(p))["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus = bus_id.lower()
+        self.proc = None
+        self.path = os.path.join("/tmp", f"nvkv_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8 or f[0].lower() != self.bus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    return rank, world, dev
+
+
+def _max_over_ranks(x, world, dev):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run_nvkv(a):
+    import torch
+
+    import nvkv
+    from nvkv import ops
+    from nvkv.decoder import QWEN3_8B, Qwen3TP, Step
+
+    rank, world, dev = _dist_setup()
+    cfg = QWEN3_8B
+    if a.layers:
+        from dataclasses import replace
+        cfg = replace(cfg, num_hidden_layers=a.layers)
+    w = workload()
+    model = Qwen3TP(cfg, rank, world, seed=0, device=dev)
+    model.allocate_kv_cache(w["num_blocks"], PAGE, fill_random=True)
+    host = {k: torch.from_numpy(np.ascontiguousarray(w[k])).pin_memory()
+            for k in ("input_ids", "positions", "slot_mapping", "cu_q", "cu_k", "block_tables")}
+    dv = {k: v.to(dev) for k, v in host.items()}
+    st = Step(dv["input_ids"], dv["positions"], dv["slot_mapping"], dv["cu_q"], dv["cu_k"],
+              dv["block_tables"], torch.arange(NUM_SEQS, device=dev), 1, w["max_k"])
+    tok_host = torch.empty(NUM_SEQS, dtype=torch.int64).pin_memory()
+
+    def step_fn():
+        return model.forward(st).argmax(-1)
+
+    for _ in range(max(1, a.warmup)):
+        tok = step_fn()
+    torch.cuda.synchronize()
+    graph = None
+    if not a.no_graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step_fn()
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            tok = step_fn()
+        for _ in range(max(3, a.warmup)):
+            graph.replay()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step_fn
+
+    props = torch.cuda.get_device_properties(dev)
+    bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    sampler = ClockSampler(bus) if rank == 0 else None
+
+    # ---- timed region: K decode steps, inputs resident in HBM ----
+    _barrier(world)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    _barrier(world)
+
+    # ---- e2e: host inputs -> H2D, step, D2H of the sampled tokens, every step ----
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    e0.record()
+    for _ in range(a.steps):
+        for k, v in host.items():
+            dv[k].copy_(v, non_blocking=True)
+        r = run()
+        tok_host.copy_(tok if r is None else r, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    _barrier(world)
+
+    # ---- roofline: per-launch CUDA events around the decode attention of every layer ----
+    q = model._bufs["q"]
+    o = model._bufs["o"]
+    ws = model._bufs["ws"]
+    reps = max(3, min(a.steps, 20))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps * cfg.num_hidden_layers)]
+    i = 0
+    for _ in range(reps):
+        for li in range(cfg.num_hidden_layers):
+            evs[i][0].record()
+            ops.paged_attention(q, model.k_caches[li], model.v_caches[li], st.cu_seqlens_q,
+                                st.cu_seqlens_k, st.block_tables, 1, w["max_k"], model.scale,
+                                out=o, workspace=ws)
+            evs[i][1].record()
+            i += 1
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in evs)
+    kern_ms = _max_over_ranks(kern_ms, world, dev)
+    assert nvkv.device_error() == 0
+    launches = model.launches_per_step(st) * a.steps
+
+    if rank == 0:
+        peak, peak_kind = load_peak()
+        nbytes = decode_bytes(w, model.hq, model.hkv)
+        achieved = nbytes / (kern_ms * 1e-3) / 1e9
+        val = NUM_SEQS * a.steps / (ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": round(val, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, random prefilled KV, random token ids)",
+            "config": {
+                "workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256, all 36 "
+                            "layers + lm_head + argmax; attention path = nvkv kernels, GEMMs = "
+                            "cuBLAS, TP collectives = NCCL",
+                "model": "Qwen3-8B", "global_batch": NUM_SEQS, "seq_len": int(w["max_k"]),
+                "parallelism": f"tp{world}", "cuda_graph": graph is not None,
+                "l2": "inputs larger than L2 (per-step KV read >> 126 MB), no flush",
+            },
+            "e2e": {"value": round(NUM_SEQS * a.steps / (ms_e2e * 1e-3), 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": NUM_SEQS * 8},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "kernel": "nvkv paged decode attention (per layer)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_launch": int(nbytes), "us_per_launch": round(kern_ms * 1e3, 2),
+                         "traffic": None},
+            "clocks": clocks,
+        }
+        if world == 1:
+            line["cpu_baseline"] = cpu_reference(max_seconds=20.0)
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU restatement of the reference path (the reference's candle-CPU route is
+# not buildable here: Rust toolchain absent), timed on the host cores.
+# ---------------------------------------------------------------------------
+
+def _cpu_sample_setup(num_tokens=32, layers=2, vocab_frac=32, seed=7):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import nvkv_oracle as O
+    from qwen3_cpu import Qwen3CPU
+    from nvkv.decoder import QWEN3_8B
+    from dataclasses import replace
+
+    cfg = replace(QWEN3_8B, num_hidden_layers=layers)
+    rng = np.random.default_rng(seed)
+    H, D, F = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
+    hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+
+    base = rng.standard_normal(1 << 20, dtype=np.float32)
+
+    def r(*shape, s=0.02):  # timing only: tile one seeded random buffer
+        n = int(np.prod(shape))
+        off = int(rng.integers(0, 1 << 19))
+        return (np.resize(np.roll(base, off), n) * np.float32(s)).reshape(shape)
+
+    wts = {"embed": r(cfg.vocab_size // vocab_frac, H, s=1.0), "norm": np.ones(H, np.float32),
+           "lm_head": r(cfg.vocab_size // vocab_frac, H)}
+    for i in range(layers):
+        wts.update({f"{i}.qkv": r((hq + 2 * hkv) * D, H), f"{i}.o": r(H, hq * D),
+                    f"{i}.gate_up": r(2 * F, H), f"{i}.down": r(H, F),
+                    f"{i}.ln1": np.ones(H, np.float32), f"{i}.ln2": np.ones(H, np.float32),
+                    f"{i}.qn": np.ones(D, np.float32), f"{i}.kn": np.ones(D, np.float32)})
+    w = workload()
+    ctx_lens = w["ctx"][:num_tokens]
+    nblk = (ctx_lens + PAGE - 1) // PAGE
+    model = Qwen3CPU(cfg, wts, int(nblk.sum()), PAGE)
+    for kc, vc in zip(model.k, model.v):
+        kc[...] = r(*kc.shape, s=1.0)
+        vc[...] = r(*vc.shape, s=1.0)
+    seqs, used = [], 0
+    for L, n in zip(ctx_lens, nblk):
+        seqs.append(O.Seq(list(rng.integers(0, 1000, int(L))), list(range(used, used + n)),
+                          int(L) - 1, 1, PAGE))
+        used += n
+    ids, pos, ctx = O.prepare_model_input(seqs, PAGE)
+    ids = ids % wts["embed"].shape[0]
+    return model, ids, pos, ctx, cfg
+
+
+def _cpu_one(model, ids, pos, ctx):
+    t0 = time.perf_counter()
+    model.forward(ids, pos, ctx)
+    return time.perf_counter() - t0
+
+
+def cpu_reference(max_seconds=20.0, reps=None, warmup=1, num_tokens=32, layers=2, vocab_frac=32):
+    """Times the CPU restatement on a bounded sample of the same decode step:
+    `num_tokens` of the 256 sequences through `layers` of the 36 layers and a
+    1/`vocab_frac` slice of lm_head; the step time is scaled by
+    (256/num_tokens) * (36/layers) for the layers and likewise for the head."""
+    model, ids, pos, ctx, cfg = _cpu_sample_setup(num_tokens, layers, vocab_frac)
+    for _ in range(warmup):
+        _cpu_one(model, ids, pos, ctx)
+    times, t_start = [], time.perf_counter()
+    while True:
+        times.append(_cpu_one(model, ids, pos, ctx))
+        if reps is not None and len(times) >= reps:
+            break
+        if reps is None and time.perf_counter() - t_start >= max_seconds:
+            break
+    t = statistics.median(times)
+    # split the sample time: lm_head slice measured alone, the rest is layers
+    h = np.zeros((num_tokens, cfg.hidden_size), np.float32)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        h @ model.w["lm_head"].T
+    t_head = (time.perf_counter() - t0) / 3
+    t_layers = max(t - t_head, 0.0)
+    step = (t_layers * (36 / layers) + t_head * vocab_frac) * (NUM_SEQS / num_tokens)
+    try:
+        import threadpoolctl
+        cores = max(i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()) or 1
+    except Exception:
+        cores = os.cpu_count()
+    return {"value": round(NUM_SEQS / step, 2), "unit": "tok/s", "cores": int(cores),
+            "kind": "port",
+            "sample": f"{num_tokens} of 256 decode tokens x {layers} of 36 layers + 1/{vocab_frac} "
+                      f"lm_head, numpy fp32 restatement (oracle/qwen3_cpu.py), median of "
+                      f"{len(times)} reps, scaled to the full step",
+            "sample_s_per_rep": round(t, 4)}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if rank != 0:
+        return
+    model, ids, pos, ctx, cfg = _cpu_sample_setup()
+    for _ in range(max(a.warmup, 1)):
+        _cpu_one(model, ids, pos, ctx)
+    cb = cpu_reference(reps=max(1, min(a.steps, 30)), warmup=0)
+    val = cb["value"]
+    line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(NUM_SEQS / val * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256 "
+                                   "(bounded CPU sample, scaled)", "model": "Qwen3-8B",
+                       "global_batch": NUM_SEQS, "seq_len": PROMPT + MAX_OUT,
+                       "parallelism": "cpu"},
+            "cpu_baseline": cb,
+            "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_nvkv(a)
+
+
+if __name__ == "__main__":
+    main()

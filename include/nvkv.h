@@ -1,0 +1,205 @@
+/*
+ * nvkv.h -- C ABI of the B200 (sm_100a) attention hot path for nanovllm_rs.
+ *
+ * One shared library, libnvkv.so, exports every function below with C
+ * linkage.  The signatures carry plain device pointers, sizes and a
+ * cudaStream_t only (no framework tensor types), so a Rust `-sys` crate,
+ * ctypes or any C caller can bind them directly.
+ *
+ * Conventions (shared by every entry point):
+ *  - Return value: NVKV_OK (0) on success, a negative NVKV_ERR_* code
+ *    otherwise.  Arguments are validated on the host before anything is
+ *    launched; on error nothing is launched and nvkv_last_error() returns a
+ *    message for the calling thread.  No C++ exception crosses the ABI.
+ *  - Every buffer belongs to the caller.  Kernels are enqueued on `stream`
+ *    and read/write the buffers asynchronously; inputs must stay alive until
+ *    the stream passes the launch (the ownership model of the reference's
+ *    candle custom ops, nanovllm_rs/src/layers/kv_cache.rs:130-151).
+ *  - The CUDA device current on the calling thread must own every pointer
+ *    (the reference binds one device per rank thread,
+ *    nanovllm_rs/src/layers/dist_util.rs:50-53).
+ *  - dtype is NVKV_DTYPE_BF16 or NVKV_DTYPE_F16 (the two dtypes the
+ *    reference's store kernel and flash-attn accept, kv_cache.rs:154-158).
+ *  - Device-side bounds checks (slot >= number of cache rows, block id >=
+ *    number of pages, position >= max_position) skip the offending access and
+ *    record an error code that nvkv_device_error() reports.
+ */
+#ifndef NVKV_H_
+#define NVKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* nvkv_stream_t; /* == cudaStream_t */
+
+#define NVKV_OK 0
+#define NVKV_ERR_INVALID_ARG (-1)   /* bad shape / null pointer / size       */
+#define NVKV_ERR_UNSUPPORTED (-2)   /* dtype, head_dim, page size, group     */
+#define NVKV_ERR_ALIGNMENT (-3)     /* pointer or stride not 16-byte aligned */
+#define NVKV_ERR_CUDA (-4)          /* a CUDA runtime/driver call failed     */
+#define NVKV_ERR_WORKSPACE (-5)     /* workspace missing or too small        */
+#define NVKV_ERR_DEVICE (-6)        /* a kernel recorded a bounds violation  */
+
+#define NVKV_DTYPE_F16 0
+#define NVKV_DTYPE_BF16 1
+
+/* Device-side error codes reported by nvkv_device_error(). */
+#define NVKV_DEVERR_NONE 0
+#define NVKV_DEVERR_SLOT_RANGE 1      /* slot_mapping[t] >= num_slots         */
+#define NVKV_DEVERR_BLOCK_RANGE 2     /* block_tables entry >= num_blocks     */
+#define NVKV_DEVERR_POSITION_RANGE 3  /* positions[t] outside [0, max_pos)    */
+#define NVKV_DEVERR_SEQLEN 4          /* q_len > k_len or lengths > maxima    */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int nvkv_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* nvkv_last_error(void);
+
+/* Reads (and if `clear` != 0 resets) the current device's error word that
+ * kernels set when a bounds check fails.  Synchronises the device.  */
+int nvkv_device_error(int* code, int clear);
+
+/* ------------------------------------------------------------------------
+ * Kernel 1: KV-cache scatter.
+ * Replaces: nanovllm_rs/src/layers/kv_cache.rs:168-190 (store_kv_cache) and
+ *           kv_cache.rs:102-161 (StoreKvCache::cuda_fwd launching the NVRTC
+ *           kernels of kv_cache.rs:9-38).
+ *
+ * k_cache[slot_mapping[t] * row_elems + i] = key[t * key_stride + i]
+ * v_cache[slot_mapping[t] * row_elems + i] = value[t * value_stride + i]
+ * for t < num_tokens, i < row_elems (= num_kv_heads * head_dim), skipping
+ * tokens whose slot is negative (the reference's padding/warm-up rule,
+ * kv_cache.rs:19-20).  Caches are [num_slots, row_elems] =
+ * [num_blocks * block_size, num_kv_heads * head_dim].  key/value may be
+ * strided views (e.g. the K and V slices of a fused qkv buffer), so no
+ * contiguous copy is needed first (the reference's force_contiguous,
+ * kv_cache.rs:175-186).  One launch writes both caches.  Bit-exact copy.
+ * ---------------------------------------------------------------------- */
+int nvkv_store_kvcache(const void* key, const void* value, void* k_cache, void* v_cache,
+                       const int64_t* slot_mapping, int64_t num_tokens, int64_t row_elems,
+                       int64_t key_stride, int64_t value_stride, int64_t num_slots,
+                       int dtype, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Kernel 4: fused qk-RMSNorm + RoPE prologue (optionally fused with kernel 1).
+ * Replaces: nanovllm_rs/src/models/qwen3.rs:128-141 (split_qkv, per-head
+ *           q_norm/k_norm, rotary_emb.forward), i.e. layers/layernorm.rs:18-25
+ *           and layers/rotary_embedding.rs:11-70.
+ *
+ * qkv: [num_tokens, (Hq + 2*Hkv) * head_dim] with row stride `qkv_stride`
+ *      elements (the output of the fused QKV projection).
+ * For each token t and head h:
+ *   x  = q or k head row;  x' = dtype(x * rsqrt(mean(x^2) + eps)) * w
+ *        (rounded to dtype after the normalise and after the weight multiply,
+ *        like the reference); skipped when q_norm_w == k_norm_w == NULL.
+ *   RoPE (NeoX half split) at positions[t] with inv_freq_i =
+ *        1 / exp((2i/D) * ln(theta)), cos/sin computed in f32 and rounded to
+ *        dtype before use, each product/sum rounded to dtype.
+ * Outputs: q_out [T, Hq, D] (required); k_out/v_out [T, Hkv, D] (optional,
+ * NULL to skip; needed only when attention runs without a KV cache).  When
+ * k_cache/v_cache/slot_mapping are non-NULL the rotated K and the V rows are
+ * also scattered into the caches exactly as nvkv_store_kvcache would.
+ * positions must lie in [0, max_position) (the reference's cos/sin table
+ * has max_position rows, rotary_embedding.rs:38-49).  head_dim must be 128.
+ * q_norm_w/k_norm_w are [head_dim] in `dtype`.
+ * ---------------------------------------------------------------------- */
+int nvkv_qknorm_rope(const void* qkv, int64_t qkv_stride, int64_t num_tokens, int num_q_heads,
+                     int num_kv_heads, int head_dim, const int64_t* positions,
+                     const void* q_norm_w, const void* k_norm_w, float eps, float rope_theta,
+                     int64_t max_position, void* q_out, void* k_out, void* v_out, void* k_cache,
+                     void* v_cache, const int64_t* slot_mapping, int64_t num_slots, int dtype,
+                     nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Kernels 2 + 3: varlen (paged) causal attention with GQA.
+ * Replaces: nanovllm_rs/src/layers/attention.rs:37-75 (the calls to
+ *           candle_flash_attn::flash_attn_varlen_paged_windowed with
+ *           window (None, Some(0)) and flash_attn_varlen(causal=true)).
+ *
+ * q:   [num_q_tokens, Hq, D] with token stride q_stride (elements); head
+ *      stride D.  num_q_tokens bounds every read of q.
+ * out: [num_q_tokens, Hq, D] contiguous.
+ * Paged (block_tables != NULL): k_cache/v_cache are [num_blocks, page_size,
+ *      Hkv, D]; key j of sequence b lives in page block_tables[b *
+ *      block_table_stride + j / page_size], row j % page_size.
+ * Contiguous (block_tables == NULL): k_cache/v_cache are [Tk, Hkv, D] and
+ *      sequence b owns rows cu_seqlens_k[b] .. cu_seqlens_k[b+1]; num_blocks
+ *      is then the row count Tk and page_size is ignored.
+ * kv_stride: elements between consecutive rows (slots / tokens) of k_cache
+ *      and v_cache; 0 means Hkv * D (dense).  A multiple of 8, so the K/V
+ *      slices of a fused qkv buffer can be attended in place.
+ * cu_seqlens_q/k: [num_seqs + 1] uint32 prefix sums (device memory).
+ * Query i of sequence b (q_len = cu_q[b+1]-cu_q[b], k_len likewise) sees key
+ * j iff j <= i + k_len - q_len when causal != 0 (all keys otherwise).
+ * Sequences with q_len == 1 run on the split-KV paged decode kernel
+ * (TMA-staged K/V, warp-shuffle softmax, LSE combine); the others run on the
+ * tcgen05 prefill kernel.  max_seqlen_q/k bound the per-sequence lengths.
+ * D must be 128; Hq % Hkv == 0 with Hq/Hkv <= 16; page_size a multiple of
+ * 128.  `workspace` must hold nvkv_paged_attention_workspace_size() bytes
+ * (16-byte aligned); it may be NULL when that size is 0.
+ * ---------------------------------------------------------------------- */
+int nvkv_paged_attention_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
+                                        int head_dim, int max_seqlen_q, int max_seqlen_k,
+                                        size_t* bytes);
+
+int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
+                         const void* k_cache, const void* v_cache, int64_t num_blocks,
+                         int64_t kv_stride, void* out,
+                         const uint32_t* cu_seqlens_q, const uint32_t* cu_seqlens_k,
+                         const uint32_t* block_tables, int64_t block_table_stride, int num_seqs,
+                         int max_seqlen_q, int max_seqlen_k, int num_q_heads, int num_kv_heads,
+                         int head_dim, int page_size, float softmax_scale, int causal,
+                         void* workspace, size_t workspace_bytes, int dtype,
+                         nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Host-side mirror of the reference's operator surface, for callers that
+ * drive the path the way nanovllm_rs's Attention does: a per-thread Context
+ * (utils/context.rs:4-54) published once per step, and an Attention object
+ * holding its layer's KV cache (layers/attention.rs:7-21).
+ * ---------------------------------------------------------------------- */
+
+/* set_context (utils/context.rs:28-50).  All pointers are device memory and
+ * must stay valid until nvkv_context_reset().  block_tables may be NULL
+ * (pure prefill, model_runner.rs:127-131); slot_mapping may be NULL when no
+ * cache is attached (warm-up).  context_lens is accepted and, like the
+ * reference, never read by attention.  Thread-local. */
+int nvkv_context_set(const uint32_t* cu_seqlens_q, const uint32_t* cu_seqlens_k, int num_seqs,
+                     int max_seqlen_q, int max_seqlen_k, const int64_t* slot_mapping,
+                     int64_t num_slot_entries, const int64_t* context_lens,
+                     const uint32_t* block_tables, int64_t block_table_stride);
+/* reset_context (utils/context.rs:52-54). */
+int nvkv_context_reset(void);
+
+typedef struct nvkv_attention* nvkv_attention_t;
+
+/* Attention::new(scale) (layers/attention.rs:14-16). */
+int nvkv_attention_create(float scale, nvkv_attention_t* out);
+int nvkv_attention_destroy(nvkv_attention_t attn);
+/* Attention::set_kv_cache (layers/attention.rs:18-21): caches are
+ * [num_blocks, page_size, num_kv_heads, head_dim] in dtype. */
+int nvkv_attention_set_kv_cache(nvkv_attention_t attn, void* k_cache, void* v_cache,
+                                int64_t num_blocks, int page_size, int num_kv_heads,
+                                int head_dim, int dtype);
+/* Attention::forward (layers/attention.rs:24-76): stores k/v through the
+ * context's slot_mapping when a cache is attached, then attends through the
+ * context's block_tables (or on k/v directly when there are none).
+ * q: [T, Hq, D] (token stride q_stride), k/v: [T, Hkv, D] (token strides
+ * k_stride/v_stride; without a cache both strides must be equal), out:
+ * [T, Hq, D] contiguous.  Scratch for split-KV is owned by the attention
+ * object and grown on demand (cudaMalloc). */
+int nvkv_attention_forward(nvkv_attention_t attn, const void* q, int64_t q_stride,
+                           const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                           int64_t num_tokens, int num_q_heads, int num_kv_heads, void* out,
+                           int dtype, nvkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVKV_H_ */

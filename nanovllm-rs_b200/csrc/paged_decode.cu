@@ -1,0 +1,427 @@
+// Kernel 2: split-KV paged decode attention (sequences with q_len == 1).
+//
+// Replaces the decode use of candle_flash_attn::flash_attn_varlen_paged_windowed
+// at nanovllm_rs/src/layers/attention.rs:43-58 (FA2, SM80 mma.sync atoms).
+// Work item = (split, kv head, sequence): one CTA streams one contiguous
+// chunk of one sequence's keys for ONE kv head and serves all g = Hq/Hkv
+// query heads of that group, so every K/V byte leaves HBM once per group.
+//
+//  * warp 4 (one elected lane) is the TMA producer: per 64-token tile it
+//    resolves the page through block_tables, then issues four
+//    cp.async.bulk.tensor loads (K and V, two 64-element halves of the
+//    128-wide head each, SWIZZLE_128B) into a 3-stage mbarrier ring;
+//  * warps 0-3 each own 16 tokens of every tile: S = Q.K^T and O += P.V run
+//    on m16n8k16 MMAs (rows = the g query heads, padded to 16), the online
+//    softmax is fp32 with quad shuffles, and P never leaves registers (the S
+//    accumulator fragment is re-packed as the A operand of P.V);
+//  * warps combine their (m, l, O) through shared memory at the end; a
+//    sequence split over several CTAs writes fp32 partials + a base-2 LSE to
+//    the workspace and nvkv_decode_combine_kernel merges them.
+//
+// Roofline: HBM.  Algorithmic bytes per (sequence, kv head) = 2*L*D*2 (K, V)
+// plus q/out rows; nothing is re-read across query heads.
+#include "common.cuh"
+
+namespace nvkv {
+
+constexpr int kDecD = 128;
+constexpr int kDecTile = 64;
+constexpr int kDecStages = 3;
+constexpr int kDecComputeWarps = 4;
+constexpr int kDecThreads = (kDecComputeWarps + 1) * 32;
+constexpr int kDecHalfBytes = kDecTile * 128;          // 64 rows x 64 elems x 2 B
+constexpr int kDecTileBytes = 2 * kDecHalfBytes;       // one K (or V) tile
+constexpr int kDecStageBytes = 2 * kDecTileBytes;      // K + V
+constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + 2 * kDecStages * 8 +
+                              kDecComputeWarps * 2 * 16 * 4 + 1024;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct DecodeParams {
+  const void* q;
+  int64_t q_stride;
+  void* out;
+  const uint32_t* cu_q;
+  const uint32_t* cu_k;
+  const uint32_t* block_tables;
+  int64_t bt_stride;
+  int64_t num_blocks;  // pages (paged) or rows (contiguous)
+  int num_q_heads;
+  int group;
+  int page_size;
+  int chunk_tokens;  // keys per split, multiple of kDecTile
+  int max_splits;
+  float scale_log2;
+  float* ws_o;    // [B][max_splits][Hq][D]
+  float* ws_lse;  // [B][max_splits][Hq]
+  int* err;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_u32(const void* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kDecThreads, 2)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                        const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
+  uint64_t* empty = full + kDecStages;
+  float* red = reinterpret_cast<float*>(empty + kDecStages);  // [warp][m|l][16]
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const uint32_t q0 = p.cu_q[b];
+  if (p.cu_q[b + 1] - q0 != 1) return;  // not a decode row: the prefill kernel owns it
+  const int k_len = (int)(p.cu_k[b + 1] - p.cu_k[b]);
+  const int nsplit = k_len > 0 ? (k_len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
+  if (split >= nsplit) return;
+  const int tok_begin = split * p.chunk_tokens;
+  const int tok_end = min(k_len, tok_begin + p.chunk_tokens);
+  const int ntiles = tok_end > tok_begin ? (tok_end - tok_begin + kDecTile - 1) / kDecTile : 0;
+  if (k_len <= 0 && threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kDecComputeWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kDecComputeWarps) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      for (int it = 0; it < ntiles; ++it) {
+        const int s = it % kDecStages;
+        const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
+        if (it >= kDecStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
+        const int j0 = tok_begin + it * kDecTile;
+        int64_t row;
+        if (p.block_tables) {
+          uint32_t page = p.block_tables[(int64_t)b * p.bt_stride + j0 / p.page_size];
+          if ((int64_t)page >= p.num_blocks) {
+            record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
+            page = 0;
+          }
+          row = (int64_t)page * p.page_size + (j0 % p.page_size);
+        } else {
+          row = (int64_t)p.cu_k[b] + j0;
+        }
+        uint8_t* st = smem + s * kDecStageBytes;
+        mbar_arrive_expect_tx(&full[s], kDecStageBytes);
+        tma_load_3d(st, &tmap_k, &full[s], 0, kvh, (int)row);
+        tma_load_3d(st + kDecHalfBytes, &tmap_k, &full[s], 64, kvh, (int)row);
+        tma_load_3d(st + kDecTileBytes, &tmap_v, &full[s], 0, kvh, (int)row);
+        tma_load_3d(st + kDecTileBytes + kDecHalfBytes, &tmap_v, &full[s], 64, kvh, (int)row);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ compute warps ------------------------------
+  const int g = p.group;
+  const int hq0 = kvh * g;
+  const int r0 = lane >> 2, r1 = r0 + 8;
+  const int cq = (lane & 3) * 2;
+  const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)q0 * p.q_stride + (int64_t)hq0 * kDecD;
+
+  uint32_t qa[8][4];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int d = kk * 16 + cq;
+    qa[kk][0] = r0 < g ? ld_u32(qrow + r0 * kDecD + d) : 0u;
+    qa[kk][1] = r1 < g ? ld_u32(qrow + r1 * kDecD + d) : 0u;
+    qa[kk][2] = r0 < g ? ld_u32(qrow + r0 * kDecD + d + 8) : 0u;
+    qa[kk][3] = r1 < g ? ld_u32(qrow + r1 * kDecD + d + 8) : 0u;
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  const int lrow = lane & 7;   // row inside an 8x8 ldmatrix tile
+  const int lmat = lane >> 3;  // which of the four 8x8 tiles this lane addresses
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int s = it % kDecStages;
+    const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
+    if (!mbar_wait(&full[s], ph, p.err)) break;
+    const uint32_t kbase = smem_u32(smem + s * kDecStageBytes);
+    const uint32_t vbase = kbase + kDecTileBytes;
+    const int tile0 = tok_begin + it * kDecTile;  // first key of the tile
+    const int wtok = warp * 16;                   // this warp's 16 keys inside the tile
+    const int valid = tok_end - (tile0 + wtok);   // keys of this slice that exist
+
+    if (valid > 0) {
+      // ---- S = Q K^T  (two n8 tiles of keys) ----
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const uint32_t krow = (uint32_t)(wtok + nt * 8 + lrow);
+#pragma unroll
+        for (int kk = 0; kk < 8; kk += 2) {
+          const uint32_t chunk = (uint32_t)(2 * kk + lmat);  // 16-byte chunk along D (0..15)
+          const uint32_t addr = kbase + (chunk >> 3) * kDecHalfBytes + sw128_offset(krow, chunk & 7);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(b0, b1, b2, b3, addr);
+          mma_16816<T>(sc[nt], qa[kk], b0, b1);
+          mma_16816<T>(sc[nt], qa[kk + 1], b2, b3);
+        }
+      }
+      // ---- masking + online softmax (rows r0 / r1, quad-reduced) ----
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool ok = (nt * 8 + cq + e) < valid;
+          sc[nt][e] = ok ? sc[nt][e] * p.scale_log2 : -INFINITY;
+          sc[nt][e + 2] = ok ? sc[nt][e + 2] * p.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, sc[nt][e]);
+          mx1 = fmaxf(mx1, sc[nt][e + 2]);
+        }
+      }
+      mx0 = warp_max_xor(warp_max_xor(mx0, 1), 2);
+      mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+      const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+      m0 = mn0;
+      m1 = mn1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sc[nt][e] = exp2f(sc[nt][e] - mu0);
+          sc[nt][e + 2] = exp2f(sc[nt][e + 2] - mu1);
+          ps0 += sc[nt][e];
+          ps1 += sc[nt][e + 2];
+        }
+      }
+      l0 = l0 * al0 + ps0;
+      l1 = l1 * al1 + ps1;
+      if (al0 != 1.f || al1 != 1.f) {
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[n][0] *= al0;
+          o[n][1] *= al0;
+          o[n][2] *= al1;
+          o[n][3] *= al1;
+        }
+      }
+      uint32_t pa[4];
+      pa[0] = DT<T>::from_f2(sc[0][0], sc[0][1]);
+      pa[1] = DT<T>::from_f2(sc[0][2], sc[0][3]);
+      pa[2] = DT<T>::from_f2(sc[1][0], sc[1][1]);
+      pa[3] = DT<T>::from_f2(sc[1][2], sc[1][3]);
+
+      // ---- O += P V  (16 n8 tiles along D) ----
+      // keys this lane's B fragments carry: wtok + cq + {0,1} (b0), + 8 (b1)
+      const uint32_t keep_lo = (cq < valid ? 0x0000ffffu : 0u) | (cq + 1 < valid ? 0xffff0000u : 0u);
+      const uint32_t keep_hi =
+          (cq + 8 < valid ? 0x0000ffffu : 0u) | (cq + 9 < valid ? 0xffff0000u : 0u);
+      const uint32_t vrow = (uint32_t)(wtok + (lmat & 1) * 8 + lrow);
+#pragma unroll
+      for (int dn = 0; dn < 16; dn += 2) {
+        const uint32_t chunk = (uint32_t)(dn + (lmat >> 1));
+        const uint32_t addr = vbase + (chunk >> 3) * kDecHalfBytes + sw128_offset(vrow, chunk & 7);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(b0, b1, b2, b3, addr);
+        b0 &= keep_lo;
+        b1 &= keep_hi;
+        b2 &= keep_lo;
+        b3 &= keep_hi;
+        mma_16816<T>(o[dn], pa, b0, b1);
+        mma_16816<T>(o[dn + 1], pa, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ------------------------------ warp combine ------------------------------
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  if ((lane & 3) == 0) {
+    red[(warp * 2 + 0) * 16 + r0] = m0;
+    red[(warp * 2 + 1) * 16 + r0] = l0;
+    red[(warp * 2 + 0) * 16 + r1] = m1;
+    red[(warp * 2 + 1) * 16 + r1] = l1;
+  }
+  named_bar_sync(1, kDecComputeWarps * 32);  // all loops done: stage memory is free
+
+  float* ofin = reinterpret_cast<float*>(smem);  // [warp][16][128] fp32 = 32 KB
+  {
+    float ms0 = -INFINITY, ms1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecComputeWarps; ++w) {
+      ms0 = fmaxf(ms0, red[(w * 2) * 16 + r0]);
+      ms1 = fmaxf(ms1, red[(w * 2) * 16 + r1]);
+    }
+    const float f0 = exp2f(m0 - (ms0 == -INFINITY ? 0.f : ms0));
+    const float f1 = exp2f(m1 - (ms1 == -INFINITY ? 0.f : ms1));
+    float* ow = ofin + warp * 16 * kDecD;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int d = n * 8 + cq;
+      *reinterpret_cast<float2*>(ow + r0 * kDecD + d) = make_float2(o[n][0] * f0, o[n][1] * f0);
+      *reinterpret_cast<float2*>(ow + r1 * kDecD + d) = make_float2(o[n][2] * f1, o[n][3] * f1);
+    }
+  }
+  named_bar_sync(1, kDecComputeWarps * 32);
+
+  const int tid = threadIdx.x;  // 0..127 == d
+  for (int r = 0; r < g; ++r) {
+    float ms = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecComputeWarps; ++w) ms = fmaxf(ms, red[(w * 2) * 16 + r]);
+    const float mu = ms == -INFINITY ? 0.f : ms;
+    float ls = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecComputeWarps; ++w) {
+      ls += red[(w * 2 + 1) * 16 + r] * exp2f(red[(w * 2) * 16 + r] - mu);
+      acc += ofin[(w * 16 + r) * kDecD + tid];
+    }
+    const float val = ls > 0.f ? acc / ls : 0.f;
+    const int hq = hq0 + r;
+    if (nsplit == 1) {
+      T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)q0 * p.num_q_heads + hq) * kDecD;
+      dst[tid] = DT<T>::from_f(val);
+    } else {
+      const int64_t wi = ((int64_t)b * p.max_splits + split) * p.num_q_heads + hq;
+      p.ws_o[wi * kDecD + tid] = val;
+      if (tid == 0) p.ws_lse[wi] = ls > 0.f ? ms + log2f(ls) : -INFINITY;
+    }
+  }
+}
+
+// Merge of the split-KV partials of one (sequence, query head): weights
+// 2^(lse_s - max lse), the standard log-sum-exp combine.
+template <typename T>
+__global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParams p) {
+  const int hq = blockIdx.x, b = blockIdx.y;
+  const uint32_t q0 = p.cu_q[b];
+  if (p.cu_q[b + 1] - q0 != 1) return;
+  const int k_len = (int)(p.cu_k[b + 1] - p.cu_k[b]);
+  const int nsplit = k_len > 0 ? (k_len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
+  if (nsplit <= 1) return;
+  const int64_t base = (int64_t)b * p.max_splits * p.num_q_heads + hq;
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.ws_lse[base + (int64_t)s * p.num_q_heads]);
+  const float mu = mx == -INFINITY ? 0.f : mx;
+  float wsum = 0.f, acc = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const int64_t wi = base + (int64_t)s * p.num_q_heads;
+    const float w = exp2f(p.ws_lse[wi] - mu);
+    wsum += w;
+    acc += w * p.ws_o[wi * kDecD + threadIdx.x];
+  }
+  T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)q0 * p.num_q_heads + hq) * kDecD;
+  dst[threadIdx.x] = DT<T>::from_f(wsum > 0.f ? acc / wsum : 0.f);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+// Split-KV plan: enough CTAs for ~3 resident waves at 2 CTAs/SM, but never
+// chunks shorter than 4 tiles (256 keys) so per-CTA setup stays amortised.
+void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
+                 int* max_splits) {
+  const int tiles = max_seqlen_k > 0 ? (max_seqlen_k + kDecTile - 1) / kDecTile : 1;
+  const int64_t items = (int64_t)num_seqs * num_kv_heads;
+  const int64_t target = 148 * 2 * 3;
+  int splits = (int)((target + items - 1) / items);
+  const int max_by_len = (tiles + 3) / 4;
+  if (splits > max_by_len) splits = max_by_len;
+  if (splits < 1) splits = 1;
+  const int tiles_per_split = (tiles + splits - 1) / splits;
+  *chunk_tokens = tiles_per_split * kDecTile;
+  *max_splits = (tiles + tiles_per_split - 1) / tiles_per_split;
+}
+
+size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k) {
+  int chunk, splits;
+  decode_plan(num_seqs, num_kv_heads, max_seqlen_k, &chunk, &splits);
+  if (splits <= 1) return 0;
+  const size_t n = (size_t)num_seqs * splits * num_q_heads;
+  return n * kDecD * sizeof(float) + n * sizeof(float) + 256;
+}
+
+int launch_paged_decode(const AttnArgs& a) {
+  int chunk, splits;
+  decode_plan(a.num_seqs, a.hkv, a.max_k, &chunk, &splits);
+  const int64_t rows = a.block_tables ? a.num_blocks * a.page : a.num_blocks;
+  CUtensorMap mk, mv;
+  int rc = encode_kv_tensor_map(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64, kDecTile,
+                                true);
+  if (rc) return rc;
+  rc = encode_kv_tensor_map(&mv, a.v_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64, kDecTile,
+                            true);
+  if (rc) return rc;
+  DecodeParams p;
+  p.q = a.q;
+  p.q_stride = a.q_stride;
+  p.out = a.out;
+  p.cu_q = a.cu_q;
+  p.cu_k = a.cu_k;
+  p.block_tables = a.block_tables;
+  p.bt_stride = a.bt_stride;
+  p.num_blocks = a.num_blocks;
+  p.num_q_heads = a.hq;
+  p.group = a.hq / a.hkv;
+  p.page_size = a.page;
+  p.chunk_tokens = chunk;
+  p.max_splits = splits;
+  p.scale_log2 = a.scale * kLog2e;
+  p.ws_o = nullptr;
+  p.ws_lse = nullptr;
+  p.err = device_error_word();
+  if (splits > 1) {
+    const size_t n = (size_t)a.num_seqs * splits * a.hq;
+    p.ws_o = reinterpret_cast<float*>(a.ws);
+    p.ws_lse = p.ws_o + n * kDecD;
+  }
+  dim3 grid(splits, a.hkv, a.num_seqs);
+  if (a.dtype == NVKV_DTYPE_BF16) {
+    auto kern = paged_decode_kernel<__nv_bfloat16>;
+    static unsigned long long attr_done_1 = 0;
+    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_1);
+    if (rc) return rc;
+    kern<<<grid, kDecThreads, kDecSmemBytes, a.stream>>>(mk, mv, p);
+    if (splits > 1)
+      decode_combine_kernel<__nv_bfloat16><<<dim3(a.hq, a.num_seqs), kDecD, 0, a.stream>>>(p);
+  } else {
+    auto kern = paged_decode_kernel<__half>;
+    static unsigned long long attr_done_2 = 0;
+    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_2);
+    if (rc) return rc;
+    kern<<<grid, kDecThreads, kDecSmemBytes, a.stream>>>(mk, mv, p);
+    if (splits > 1)
+      decode_combine_kernel<__half><<<dim3(a.hq, a.num_seqs), kDecD, 0, a.stream>>>(p);
+  }
+  return check_cuda(cudaGetLastError(), "paged decode launch");
+}
+
+}  // namespace nvkv

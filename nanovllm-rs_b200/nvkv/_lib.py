@@ -1,0 +1,91 @@
+"""ctypes binding of libnvkv.so (the C ABI declared in include/nvkv.h).
+
+The library is loaded from this directory only.  There is no fallback: if
+the shared object is missing or does not export a declared symbol, importing
+the package raises, so a test or benchmark can never pass on a CPU or
+PyTorch stand-in.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnvkv.so")
+
+OK = 0
+ERR_INVALID_ARG = -1
+ERR_UNSUPPORTED = -2
+ERR_ALIGNMENT = -3
+ERR_CUDA = -4
+ERR_WORKSPACE = -5
+ERR_DEVICE = -6
+
+DTYPE_F16 = 0
+DTYPE_BF16 = 1
+
+DEVERR_NONE = 0
+DEVERR_SLOT_RANGE = 1
+DEVERR_BLOCK_RANGE = 2
+DEVERR_POSITION_RANGE = 3
+DEVERR_SEQLEN = 4
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> argtypes, in the order of include/nvkv.h
+SIGNATURES = {
+    "nvkv_version": [],
+    "nvkv_last_error": [],
+    "nvkv_device_error": [ctypes.POINTER(_i32), _i32],
+    "nvkv_store_kvcache": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p],
+    "nvkv_qknorm_rope": [_p, _i64, _i64, _i32, _i32, _i32, _p, _p, _p, _f32, _f32, _i64, _p, _p,
+                         _p, _p, _p, _p, _i64, _i32, _p],
+    "nvkv_paged_attention_workspace_size": [_i32, _i32, _i32, _i32, _i32, _i32,
+                                            ctypes.POINTER(_sz)],
+    "nvkv_paged_attention": [_p, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _i32,
+                             _i32, _i32, _i32, _i32, _i32, _f32, _i32, _p, _sz, _i32, _p],
+    "nvkv_context_set": [_p, _p, _i32, _i32, _i32, _p, _i64, _p, _p, _i64],
+    "nvkv_context_reset": [],
+    "nvkv_attention_create": [_f32, ctypes.POINTER(_p)],
+    "nvkv_attention_destroy": [_p],
+    "nvkv_attention_set_kv_cache": [_p, _p, _p, _i64, _i32, _i32, _i32, _i32],
+    "nvkv_attention_forward": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _p, _i32, _p],
+}
+
+
+class NvkvError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"nvkv error {code}: {msg}")
+        self.code = code
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python nanovllm-rs_b200/build.py` "
+            "(there is no CPU fallback for this path)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)  # AttributeError if the symbol is not exported
+        fn.argtypes = argtypes
+        fn.restype = ctypes.c_char_p if name == "nvkv_last_error" else _i32
+    return lib
+
+
+lib = _load()
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        raise NvkvError(rc, lib.nvkv_last_error().decode(errors="replace"))
+
+
+def device_error(clear: bool = True) -> int:
+    """Reads (and by default clears) the current device's bounds-check word."""
+    code = _i32(0)
+    check(lib.nvkv_device_error(ctypes.byref(code), 1 if clear else 0))
+    return code.value

@@ -1,0 +1,274 @@
+"""Qwen3-shaped tensor-parallel decoder driving the nvkv hot path.
+
+This is the caller side of the path (models/qwen3.rs:126-146,179-183,226-297,
+layers/linear.rs, layers/embed_head.rs) restated with torch for everything
+that is NOT one of the path's kernels: the projections are cuBLAS GEMMs, the
+residual RMSNorm / SiLU*mul are torch elementwise ops, and the tensor-parallel
+collectives are NCCL through torch.distributed.  Per layer the attention hot
+path is exactly two nvkv launches: nvkv_qknorm_rope (split_qkv + q/k RMSNorm
++ RoPE + KV-cache store, fused) and nvkv_paged_attention (split-KV decode or
+tcgen05 prefill).
+
+Tensor-parallel layout (one process per GPU), as the reference shards it:
+  * qkv_proj   column-parallel, local rows [q_r ; k_r ; v_r]  (linear.rs:214-281)
+  * o_proj     row-parallel + all-reduce                      (linear.rs:153-212)
+  * gate_up    merged column-parallel [gate_r ; up_r]          (linear.rs:78-151)
+  * down_proj  row-parallel + all-reduce
+  * embedding  vocab-parallel, masked lookup + all-reduce      (embed_head.rs:47-60)
+  * lm_head    vocab-parallel, all-gather of the logit shards  (embed_head.rs:89-119)
+Weights are random-initialised from a seed per tensor (no checkpoints exist
+here); every rank draws the same full tensor and keeps its shard, so any TP
+degree computes the same model.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+@dataclass
+class Qwen3Config:
+    """The config.json fields the reference reads (config.rs:5-27)."""
+
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    intermediate_size: int
+    vocab_size: int = 151936
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    max_position_embeddings: int = 40960
+    tie_word_embeddings: bool = False
+
+
+QWEN3_0_6B = Qwen3Config(1024, 28, 16, 8, 3072, tie_word_embeddings=True)
+QWEN3_4B = Qwen3Config(2560, 36, 32, 8, 9728, tie_word_embeddings=True)
+QWEN3_8B = Qwen3Config(4096, 36, 32, 8, 12288)
+QWEN3_32B = Qwen3Config(5120, 64, 64, 8, 25600)
+
+
+# ---------------------------------------------------------------------------
+# TP sharding helpers (pure host logic; unit-tested with gloo on CPU)
+# ---------------------------------------------------------------------------
+
+def divide(n: int, tp: int) -> int:
+    if n % tp:
+        raise ValueError(f"{n} is not divisible by tp={tp}")  # qwen3.rs:61,65
+    return n // tp
+
+
+def shard_qkv(wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, rank: int, tp: int):
+    """QKVParallelLinear::weight_loader (linear.rs:253-280): rank r keeps the
+    r-th slice of each of q, k, v along the output dim, fused [q;k;v]."""
+    q = wq.narrow(0, rank * divide(wq.size(0), tp), divide(wq.size(0), tp))
+    k = wk.narrow(0, rank * divide(wk.size(0), tp), divide(wk.size(0), tp))
+    v = wv.narrow(0, rank * divide(wv.size(0), tp), divide(wv.size(0), tp))
+    return torch.cat([q, k, v], 0).contiguous()
+
+
+def shard_merged(ws: List[torch.Tensor], rank: int, tp: int) -> torch.Tensor:
+    """MergedColumnParallelLinear (linear.rs:109-151): [gate_r ; up_r]."""
+    return torch.cat([w.narrow(0, rank * divide(w.size(0), tp), divide(w.size(0), tp))
+                      for w in ws], 0).contiguous()
+
+
+def shard_row(w: torch.Tensor, rank: int, tp: int) -> torch.Tensor:
+    """RowParallelLinear::weight_loader (linear.rs:173-185): input-dim slice."""
+    n = divide(w.size(1), tp)
+    return w.narrow(1, rank * n, n).contiguous()
+
+
+def shard_vocab(w: torch.Tensor, rank: int, tp: int) -> torch.Tensor:
+    """VocabParallelEmbedding::weight_loader (embed_head.rs:42-45)."""
+    n = divide(w.size(0), tp)
+    return w.narrow(0, rank * n, n).contiguous()
+
+
+def vocab_parallel_embed(ids: torch.Tensor, w_local: torch.Tensor, rank: int, group=None):
+    """embed_head.rs:47-60: masked local lookup, then sum over ranks."""
+    n = w_local.size(0)
+    start = rank * n
+    mask = (ids >= start) & (ids < start + n)
+    y = torch.nn.functional.embedding((ids - start) * mask, w_local) * mask.unsqueeze(-1)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(y, group=group)
+    return y
+
+
+def gather_logits(local: torch.Tensor, group=None) -> torch.Tensor:
+    """gather_concat (dist_util.rs:145-159): all-gather the vocab shards and
+    concatenate along the vocab dim."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return local
+    ws = dist.get_world_size(group)
+    parts = [torch.empty_like(local) for _ in range(ws)]
+    dist.all_gather(parts, local.contiguous(), group=group)
+    return torch.cat(parts, dim=-1)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """layernorm.rs:18-25: f32 statistics, cast, then x weight."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return y.to(x.dtype) * w
+
+
+def residual_rms_norm(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float):
+    """layernorm.rs:27-42: returns (normed, new_residual)."""
+    xf = x.float() + res.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return y.to(x.dtype) * w, xf.to(x.dtype)
+
+
+# ---------------------------------------------------------------------------
+# Step metadata on the device (what ModelRunner::prepare_model_input uploads)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Step:
+    input_ids: torch.Tensor     # [T] int64
+    positions: torch.Tensor     # [T] int64
+    slot_mapping: torch.Tensor  # [T] int64
+    cu_seqlens_q: torch.Tensor  # [B+1] int32
+    cu_seqlens_k: torch.Tensor  # [B+1] int32
+    block_tables: torch.Tensor  # [B, W] int32
+    last_idx: torch.Tensor      # [B] int64: row of each sequence's last token
+    max_seqlen_q: int
+    max_seqlen_k: int
+
+
+class Qwen3TP:
+    """One rank of a TP-sharded Qwen3 decoder whose attention is the nvkv path."""
+
+    def __init__(self, cfg: Qwen3Config, rank: int = 0, tp: int = 1, seed: int = 0,
+                 dtype=torch.bfloat16, device="cuda", init_scale: float = 1.0, group=None):
+        self.cfg, self.rank, self.tp, self.group = cfg, rank, tp, group
+        self.dtype, self.device = dtype, torch.device(device)
+        self.hq = divide(cfg.num_attention_heads, tp)
+        self.hkv = divide(cfg.num_key_value_heads, tp)
+        self.ffn = divide(cfg.intermediate_size, tp)
+        self.scale = cfg.head_dim ** -0.5  # qwen3.rs:71
+        self._seed = seed
+        self._n = 0
+        H, D = cfg.hidden_size, cfg.head_dim
+
+        def full(rows, cols, std):
+            self._n += 1
+            g = torch.Generator(device=self.device).manual_seed(seed * 1000003 + self._n)
+            return (torch.randn(rows, cols, generator=g, device=self.device) * std).to(dtype)
+
+        def norm_w(n):
+            self._n += 1
+            g = torch.Generator(device=self.device).manual_seed(seed * 1000003 + self._n)
+            return (1.0 + 0.1 * torch.randn(n, generator=g, device=self.device)).to(dtype)
+
+        s_in = init_scale / math.sqrt(H)
+        emb = full(cfg.vocab_size, H, 1.0)
+        self.embed = shard_vocab(emb, rank, tp)
+        self.layers = []
+        for _ in range(cfg.num_hidden_layers):
+            L = {}
+            wq = full(cfg.num_attention_heads * D, H, s_in)
+            wk = full(cfg.num_key_value_heads * D, H, s_in)
+            wv = full(cfg.num_key_value_heads * D, H, s_in)
+            L["qkv"] = shard_qkv(wq, wk, wv, rank, tp)
+            del wq, wk, wv
+            L["o"] = shard_row(full(H, cfg.num_attention_heads * D,
+                                    init_scale / math.sqrt(cfg.num_attention_heads * D)), rank, tp)
+            L["gate_up"] = shard_merged([full(cfg.intermediate_size, H, s_in),
+                                         full(cfg.intermediate_size, H, s_in)], rank, tp)
+            L["down"] = shard_row(full(H, cfg.intermediate_size,
+                                       init_scale / math.sqrt(cfg.intermediate_size)), rank, tp)
+            L["ln1"], L["ln2"] = norm_w(H), norm_w(H)
+            L["qn"], L["kn"] = norm_w(D), norm_w(D)
+            self.layers.append(L)
+        self.norm = norm_w(H)
+        lm = emb if cfg.tie_word_embeddings else full(cfg.vocab_size, H, s_in)
+        self.lm_head = shard_vocab(lm, rank, tp)  # tie_weights (qwen3.rs:334-338)
+        del emb, lm
+        self.k_caches: List[torch.Tensor] = []
+        self.v_caches: List[torch.Tensor] = []
+        self._bufs = {}
+
+    # ---- KV pool (model_runner.rs:286-303): per layer [Nb, P, Hkv/tp, D] ----
+    def allocate_kv_cache(self, num_blocks: int, block_size: int = 256, fill_random: bool = False,
+                          seed: int = 1) -> None:
+        shape = (num_blocks, block_size, self.hkv, self.cfg.head_dim)
+        self.k_caches, self.v_caches = [], []
+        g = torch.Generator(device=self.device).manual_seed(seed * 7919 + self.rank)
+        for _ in range(self.cfg.num_hidden_layers):
+            if fill_random:
+                k = torch.randn(shape, generator=g, device=self.device, dtype=self.dtype)
+                v = torch.randn(shape, generator=g, device=self.device, dtype=self.dtype)
+            else:
+                k = torch.zeros(shape, device=self.device, dtype=self.dtype)
+                v = torch.zeros(shape, device=self.device, dtype=self.dtype)
+            self.k_caches.append(k)
+            self.v_caches.append(v)
+
+    def _buf(self, name, shape, dtype=None):
+        b = self._bufs.get(name)
+        if b is None or b.shape != torch.Size(shape):
+            b = torch.empty(shape, device=self.device, dtype=dtype or self.dtype)
+            self._bufs[name] = b
+        return b
+
+    def _all_reduce(self, x):
+        if self.tp > 1:
+            dist.all_reduce(x, group=self.group)
+        return x
+
+    @torch.no_grad()
+    def forward(self, st: Step) -> torch.Tensor:
+        """Qwen3ForCausalLM::forward + compute_logits (qwen3.rs:285-297,
+        embed_head.rs:89-119): returns the full-vocab logits of each
+        sequence's last token, [B, V] (float32)."""
+        cfg = self.cfg
+        T = st.input_ids.numel()
+        D = cfg.head_dim
+        h = vocab_parallel_embed(st.input_ids, self.embed, self.rank, self.group)
+        q_buf = self._buf("q", (T, self.hq, D))
+        o_buf = self._buf("o", (T, self.hq, D))
+        ws_n = ops.workspace_size(st.cu_seqlens_q.numel() - 1, self.hq, self.hkv, st.max_seqlen_q,
+                                  st.max_seqlen_k, D)
+        ws = self._buf("ws", (max(ws_n, 16),), torch.uint8)
+        residual = None
+        for li, L in enumerate(self.layers):
+            if residual is None:
+                x, residual = rms_norm(h, L["ln1"], cfg.rms_norm_eps), h
+            else:
+                x, residual = residual_rms_norm(h, residual, L["ln1"], cfg.rms_norm_eps)
+            qkv = torch.matmul(x, L["qkv"].t())
+            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"],
+                            cfg.rms_norm_eps, cfg.rope_theta, cfg.max_position_embeddings, D,
+                            k_cache=self.k_caches[li], v_cache=self.v_caches[li],
+                            slot_mapping=st.slot_mapping, q_out=q_buf)
+            ops.paged_attention(q_buf, self.k_caches[li], self.v_caches[li], st.cu_seqlens_q,
+                                st.cu_seqlens_k, st.block_tables, st.max_seqlen_q,
+                                st.max_seqlen_k, self.scale, out=o_buf, workspace=ws)
+            a = self._all_reduce(torch.matmul(o_buf.view(T, -1), L["o"].t()))
+            x, residual = residual_rms_norm(a, residual, L["ln2"], cfg.rms_norm_eps)
+            gu = torch.matmul(x, L["gate_up"].t())
+            act = torch.nn.functional.silu(gu[:, :self.ffn]) * gu[:, self.ffn:]
+            h = self._all_reduce(torch.matmul(act, L["down"].t()))
+        h, _ = residual_rms_norm(h, residual, self.norm, cfg.rms_norm_eps)
+        last = h.index_select(0, st.last_idx)
+        logits = torch.matmul(last, self.lm_head.t()).float()
+        return gather_logits(logits, self.group)
+
+    def launches_per_step(self, st: Step) -> int:
+        """nvkv kernel launches one forward issues: per layer the prologue,
+        the decode kernel, the combine kernel when the split-KV plan splits,
+        and the prefill kernel when any sequence has q_len > 1."""
+        B = st.cu_seqlens_q.numel() - 1
+        split = ops.workspace_size(B, self.hq, self.hkv, st.max_seqlen_q, st.max_seqlen_k) > 0
+        per = 2 + (1 if split else 0) + (1 if st.max_seqlen_q > 1 else 0)
+        return per * self.cfg.num_hidden_layers

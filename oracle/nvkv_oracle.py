@@ -1,0 +1,389 @@
+"""CPU restatement of nanovllm_rs's per-layer attention hot path.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker that the CUDA path is
+compared against.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it; the
+product path (``nanovllm-rs_b200/``) never does, and fails loudly when its CUDA
+library is missing instead of falling back to anything here.
+
+Parity status: UNPINNED with respect to reference-produced numbers.  The
+reference (Athe-kunal/nanovllm-rs) is Rust on candle 0.11 and cannot be built or
+run in this container (no cargo/rustc, no vendored crates), and its only
+known-answer probe (``nanovllm_rs/src/bin/repro.rs``) prints diffs without
+asserting or recording values.  What pins this restatement instead:
+
+* KAT-1: the ``repro.rs`` input generator restated bit-for-bit
+  (``repro_inputs``); the store must reproduce ``k_full`` exactly
+  (``cache_write_diff == 0``, repro.rs:116-121) and the paged attention must
+  equal repro.rs's own ``manual_attention`` (repro.rs:6-32, restated separately
+  in ``tests/golden/make_golden.py``).
+* KAT-2: hand-computed slot mappings for ``prepare_model_input``
+  (model_runner.rs:108-124) committed as literal arrays.
+
+Third-party arithmetic the reference delegates to (not under the reference
+tree; pinned in ``nanovllm_rs/Cargo.lock``): candle-flash-attn 0.11.0 (FA2
+``flash_attn_varlen`` / ``flash_attn_varlen_paged_windowed``), candle-nn 0.11.0
+(``flash_attn_varlen_unfused``), candle-core 0.11.0 (elementwise kernels),
+half 2.7.1 (bf16 round-to-nearest-even).  Their published semantics are
+restated here: exact softmax attention, causal mask aligned bottom-right
+(key j visible to query i iff ``j <= i + k_len - q_len``), GQA head h reads kv
+head ``h // (Hq // Hkv)``.
+
+Every array is numpy.  bf16 values are carried as float32 arrays whose values
+are bf16-representable; ``bf16_bits``/``from_bf16_bits`` convert to and from
+the 16-bit storage pattern.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence as Seq_, Tuple
+
+import numpy as np
+
+# --------------------------------------------------------------------------
+# dtype helpers
+# --------------------------------------------------------------------------
+
+
+def round_bf16(x) -> np.ndarray:
+    """float32 -> nearest-even bf16 value, returned as float32.
+
+    Follows half 2.7.1 ``bf16::from_f32`` (round to nearest, ties to even; NaN
+    stays NaN), which candle uses for every ``to_dtype(BF16)``.
+    """
+    x = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    u = x.view(np.uint32).astype(np.uint64)
+    bias = ((u >> 16) & 1) + 0x7FFF
+    r = (((u + bias) >> 16) << 16).astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), np.float32(np.nan), r).astype(np.float32)
+
+
+def bf16_bits(x) -> np.ndarray:
+    """bf16 storage bits (uint16) of float32 values (rounded RNE first)."""
+    r = round_bf16(x)
+    return (r.view(np.uint32) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(b) -> np.ndarray:
+    b = np.asarray(b, dtype=np.uint16)
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def round_to(x, dtype: str) -> np.ndarray:
+    """Round float32 values to the activation dtype ('bf16', 'f16' or 'f32')."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "bf16":
+        return round_bf16(x)
+    if dtype == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    if dtype == "f32":
+        return x
+    raise ValueError(f"unsupported dtype {dtype}")
+
+
+# --------------------------------------------------------------------------
+# a1: KV-cache scatter
+# --------------------------------------------------------------------------
+
+
+def store_kvcache(key, value, k_cache, v_cache, slot_mapping) -> None:
+    """In-place row scatter; nanovllm_rs/src/layers/kv_cache.rs:13-24, 168-190.
+
+    ``key``/``value``: [T, Hkv, D] (or [T, d]).  Caches: [Nb, P, Hkv, D],
+    viewed as [Nb*P, Hkv*D].  Row t goes to cache row ``slot_mapping[t]``;
+    rows whose slot is negative are skipped (kv_cache.rs:19-20).  Works on any
+    numpy dtype (uint16 bit patterns included), so it is bit-exact by
+    construction.
+    """
+    T = key.shape[0]
+    kc = k_cache.reshape(-1, int(np.prod(k_cache.shape[2:])))
+    vc = v_cache.reshape(-1, int(np.prod(v_cache.shape[2:])))
+    k2 = key.reshape(T, -1)
+    v2 = value.reshape(T, -1)
+    if k2.shape[1] != kc.shape[1] or v2.shape[1] != vc.shape[1]:
+        raise ValueError("store_kvcache: cache per-slot width does not match src width")
+    slots = np.asarray(slot_mapping, dtype=np.int64)
+    valid = slots >= 0
+    if np.any(slots[valid] >= kc.shape[0]):
+        raise IndexError("store_kvcache: slot out of range")
+    kc[slots[valid]] = k2[valid]
+    vc[slots[valid]] = v2[valid]
+
+
+# --------------------------------------------------------------------------
+# a8: metadata (Sequence -> Context)
+# --------------------------------------------------------------------------
+
+
+@dataclass
+class Seq:
+    """The fields of ``Sequence`` (engine/sequence.rs:22-36) the runner reads."""
+
+    token_ids: List[int]
+    block_table: List[int] = field(default_factory=list)
+    num_cached_tokens: int = 0
+    num_new_tokens: int = 0
+    block_size: int = 256
+
+    def __len__(self) -> int:  # sequence.rs:66-68
+        return len(self.token_ids)
+
+    def num_context_tokens(self) -> int:  # sequence.rs:82-84
+        return self.num_cached_tokens + self.num_new_tokens
+
+    def num_cached_blocks(self) -> int:  # sequence.rs:99-101
+        return self.num_cached_tokens // self.block_size
+
+
+@dataclass
+class Context:
+    """utils/context.rs:4-13 (host copy of every field)."""
+
+    cu_seqlens_q: np.ndarray
+    cu_seqlens_k: np.ndarray
+    max_seqlen_q: int
+    max_seqlen_k: int
+    slot_mapping: np.ndarray
+    context_lens: np.ndarray
+    block_tables: Optional[np.ndarray]
+    seq_need_compute_logits: np.ndarray
+
+
+def prepare_block_tables(seqs: Seq_[Seq]) -> np.ndarray:
+    """engine/model_runner.rs:53-67: [B, max_blocks] uint32, padded with 0."""
+    max_len = max(len(s.block_table) for s in seqs)
+    bt = np.zeros((len(seqs), max_len), dtype=np.uint32)
+    for i, s in enumerate(seqs):
+        bt[i, : len(s.block_table)] = s.block_table
+    return bt
+
+
+def prepare_model_input(seqs: Seq_[Seq], block_size: int) -> Tuple[np.ndarray, np.ndarray, Context]:
+    """engine/model_runner.rs:69-160.  Returns (input_ids, positions, context)."""
+    input_ids: List[int] = []
+    positions: List[int] = []
+    cu_q = [0]
+    cu_k = [0]
+    max_q = 0
+    max_k = 0
+    slots: List[int] = []
+    context_lens: List[int] = []
+    need_logits: List[int] = []
+    for idx, s in enumerate(seqs):
+        n_ctx = s.num_context_tokens()
+        if len(s) == n_ctx and s.block_table:  # :85-87
+            need_logits.append(idx)
+        context_lens.append(n_ctx)
+        input_ids.extend(s.token_ids[s.num_cached_tokens:n_ctx])  # :89-93
+        positions.extend(range(s.num_cached_tokens, n_ctx))  # :94
+        cu_q.append(cu_q[-1] + s.num_new_tokens)  # :96-99
+        cu_k.append(cu_k[-1] + n_ctx)
+        max_q = max(max_q, s.num_new_tokens)
+        max_k = max(max_k, n_ctx)
+        if not s.block_table:  # warmup: no slots (:103-106)
+            continue
+        first = s.num_cached_blocks()
+        last = len(s.block_table) - 1
+        for i in range(first, len(s.block_table)):  # :108-124
+            b = s.block_table[i]
+            start = b * block_size + (s.num_cached_tokens % block_size if i == first else 0)
+            if i == last and n_ctx % block_size != 0:
+                end = b * block_size + n_ctx % block_size
+            else:
+                end = (b + 1) * block_size
+            slots.extend(range(start, end))
+    block_tables = prepare_block_tables(seqs) if cu_k[-1] > cu_q[-1] else None  # :127-131
+    ctx = Context(
+        cu_seqlens_q=np.asarray(cu_q, dtype=np.uint32),
+        cu_seqlens_k=np.asarray(cu_k, dtype=np.uint32),
+        max_seqlen_q=max_q,
+        max_seqlen_k=max_k,
+        slot_mapping=np.asarray(slots, dtype=np.int64),
+        context_lens=np.asarray(context_lens, dtype=np.int64),
+        block_tables=block_tables,
+        seq_need_compute_logits=np.asarray(need_logits, dtype=np.int64),
+    )
+    return np.asarray(input_ids, dtype=np.int64), np.asarray(positions, dtype=np.int64), ctx
+
+
+# --------------------------------------------------------------------------
+# a4: paged gather + causal varlen attention (the fallback route's semantics)
+# --------------------------------------------------------------------------
+
+
+def gather_paged_kv(k_cache, v_cache, block_table_row, seqlen_k: int, page_size: int):
+    """layers/attention.rs:143-164: token-ordered rows of one sequence."""
+    slots: List[int] = []
+    for b in block_table_row:
+        for s in range(page_size):
+            if len(slots) == seqlen_k:
+                break
+            slots.append(int(b) * page_size + s)
+        if len(slots) == seqlen_k:
+            break
+    hkv, d = k_cache.shape[2], k_cache.shape[3]
+    idx = np.asarray(slots, dtype=np.int64)
+    return k_cache.reshape(-1, hkv, d)[idx], v_cache.reshape(-1, hkv, d)[idx]
+
+
+def causal_attention_one(q, k, v, scale: float, causal: bool = True, acc=np.float64):
+    """Exact softmax attention for one sequence, GQA by head grouping.
+
+    q: [q_len, Hq, D]; k, v: [k_len, Hkv, D].  Causal mask aligned bottom-right:
+    key j is visible to query i iff j <= i + (k_len - q_len) (the cache-offset
+    case candle_nn's unfused varlen path and FA2's causal mode both implement,
+    layers/attention.rs:78-84).  Returns float32 [q_len, Hq, D].
+    """
+    q_len, hq, d = q.shape
+    k_len, hkv, _ = k.shape
+    if q_len == 0:
+        return np.zeros((0, hq, d), np.float32)
+    g = hq // hkv
+    qh = q.astype(acc).reshape(q_len, hkv, g, d).transpose(1, 2, 0, 3)  # [hkv,g,q,d]
+    kh = k.astype(acc).transpose(1, 2, 0)  # [hkv,d,k]
+    vh = v.astype(acc).transpose(1, 0, 2)  # [hkv,k,d]
+    s = np.matmul(qh, kh[:, None]) * scale  # [hkv,g,q,k]
+    if causal:
+        i = np.arange(q_len)[:, None]
+        j = np.arange(k_len)[None, :]
+        s = np.where(j <= i + (k_len - q_len), s, -np.inf)
+    m = np.max(s, axis=-1, keepdims=True)
+    m = np.where(np.isfinite(m), m, 0.0)
+    p = np.exp(s - m)
+    l = np.sum(p, axis=-1, keepdims=True)
+    o = np.matmul(p, vh[:, None]) / np.where(l > 0, l, 1.0)  # [hkv,g,q,d]
+    return o.transpose(2, 0, 1, 3).reshape(q_len, hq, d).astype(np.float32)
+
+
+def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, causal=True, acc=np.float64):
+    """flash_attn_varlen semantics on contiguous K/V (layers/attention.rs:60-74)."""
+    out = np.zeros(q.shape, np.float32)
+    for b in range(len(cu_seqlens_q) - 1):
+        q0, q1 = int(cu_seqlens_q[b]), int(cu_seqlens_q[b + 1])
+        k0, k1 = int(cu_seqlens_k[b]), int(cu_seqlens_k[b + 1])
+        out[q0:q1] = causal_attention_one(q[q0:q1], k[k0:k1], v[k0:k1], scale, causal, acc)
+    return out
+
+
+def paged_attention(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables, scale,
+                    causal=True, acc=np.float64):
+    """Paged route (layers/attention.rs:38-59) computed the fallback way
+    (attention.rs:105-136): gather each sequence's rows, then attend."""
+    out = np.zeros(q.shape, np.float32)
+    page = k_cache.shape[1]
+    for b in range(len(cu_seqlens_q) - 1):
+        q0, q1 = int(cu_seqlens_q[b]), int(cu_seqlens_q[b + 1])
+        k_len = int(cu_seqlens_k[b + 1]) - int(cu_seqlens_k[b])
+        kb, vb = gather_paged_kv(k_cache, v_cache, block_tables[b], k_len, page)
+        out[q0:q1] = causal_attention_one(q[q0:q1], kb, vb, scale, causal, acc)
+    return out
+
+
+def attention_forward(q, k, v, ctx: Context, k_cache, v_cache, scale, acc=np.float64):
+    """Attention::forward (layers/attention.rs:85-137): store, then attend
+    through the block table when present, else on the fresh K/V."""
+    if k_cache is not None and v_cache is not None:
+        store_kvcache(k, v, k_cache, v_cache, ctx.slot_mapping)
+    if ctx.block_tables is not None:
+        return paged_attention(q, k_cache, v_cache, ctx.cu_seqlens_q, ctx.cu_seqlens_k,
+                               ctx.block_tables, scale, True, acc)
+    return varlen_attention(q, k, v, ctx.cu_seqlens_q, ctx.cu_seqlens_k, scale, True, acc)
+
+
+# --------------------------------------------------------------------------
+# a5 / a6: qk-RMSNorm and RoPE with the reference's rounding points
+# --------------------------------------------------------------------------
+
+
+def rms_norm(x, weight, eps: float, dtype: str) -> np.ndarray:
+    """layers/layernorm.rs:18-25.
+
+    f32 math; ``x * rsqrt(mean(x^2) + eps)`` is rounded to the activation
+    dtype *before* the weight multiply, whose product is rounded again.
+    """
+    xf = np.asarray(x, np.float32)
+    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
+    inv = np.float32(1.0) / np.sqrt(var + np.float32(eps))
+    normed = round_to(xf * inv, dtype)
+    return round_to(normed * np.asarray(weight, np.float32), dtype)
+
+
+def rope_inv_freq(head_dim: int, base: float) -> np.ndarray:
+    """layers/rotary_embedding.rs:31-37: 1/exp((2i/D)*ln(base)) in f32."""
+    exponent = np.arange(0, head_dim, 2, dtype=np.float32) / np.float32(head_dim)
+    ln_base = np.float32(math.log(base))
+    return (np.float32(1.0) / np.exp(exponent * ln_base)).astype(np.float32)
+
+
+def rope_cos_sin(positions, head_dim: int, base: float) -> Tuple[np.ndarray, np.ndarray]:
+    """rotary_embedding.rs:38-49 + index_select (:60): f32 cos/sin rows."""
+    inv = rope_inv_freq(head_dim, base)
+    t = np.asarray(positions, dtype=np.int64).astype(np.float32)
+    freqs = (t[:, None] * inv[None, :]).astype(np.float32)
+    return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
+
+
+def apply_rotary_emb(x, cos, sin, dtype: str) -> np.ndarray:
+    """rotary_embedding.rs:11-26 (NeoX half split), rounding after each op."""
+    half = x.shape[-1] // 2
+    x1 = x[..., :half]
+    x2 = x[..., half:]
+    y1 = round_to(round_to(x1 * cos, dtype) - round_to(x2 * sin, dtype), dtype)
+    y2 = round_to(round_to(x2 * cos, dtype) + round_to(x1 * sin, dtype), dtype)
+    return np.concatenate([y1, y2], axis=-1)
+
+
+def rope_forward(positions, q, k, head_dim: int, base: float, dtype: str):
+    """rotary_embedding.rs:59-70: cos/sin cast to the activation dtype first."""
+    cos, sin = rope_cos_sin(positions, head_dim, base)
+    cos = round_to(cos, dtype)[:, None, :]
+    sin = round_to(sin, dtype)[:, None, :]
+    return apply_rotary_emb(q, cos, sin, dtype), apply_rotary_emb(k, cos, sin, dtype)
+
+
+def qknorm_rope(qkv, positions, num_q_heads, num_kv_heads, head_dim, q_w, k_w, eps, theta,
+                dtype: str):
+    """Qwen3Attention::forward prologue (models/qwen3.rs:126-141):
+    split_qkv (:33-38) -> per-head q/k RMSNorm -> RoPE.  Returns (q, k, v)."""
+    T = qkv.shape[0]
+    qs = num_q_heads * head_dim
+    ks = num_kv_heads * head_dim
+    q = np.asarray(qkv[:, :qs], np.float32).reshape(T, num_q_heads, head_dim)
+    k = np.asarray(qkv[:, qs:qs + ks], np.float32).reshape(T, num_kv_heads, head_dim)
+    v = np.asarray(qkv[:, qs + ks:qs + 2 * ks], np.float32).reshape(T, num_kv_heads, head_dim)
+    if q_w is not None:
+        q = rms_norm(q, q_w, eps, dtype)
+        k = rms_norm(k, k_w, eps, dtype)
+    q, k = rope_forward(positions, q, k, head_dim, theta, dtype)
+    return q, k, v
+
+
+# --------------------------------------------------------------------------
+# KAT-1 inputs: nanovllm_rs/src/bin/repro.rs
+# --------------------------------------------------------------------------
+
+REPRO_N_HEADS = 16
+REPRO_N_KV_HEADS = 8
+REPRO_HEAD_DIM = 128
+REPRO_BLOCK_SIZE = 256
+REPRO_PRIOR_LEN = 6
+
+
+def repro_mk(seed: np.float32, n: int, h: int, head_dim: int = REPRO_HEAD_DIM) -> np.ndarray:
+    """repro.rs:50-53: data[i] = ((i*seed) % 17 - 8) / 8 in f32, then bf16."""
+    i = np.arange(n * h * head_dim, dtype=np.float32)
+    data = (np.fmod(i * np.float32(seed), np.float32(17.0)) - np.float32(8.0)) / np.float32(8.0)
+    return round_bf16(data.astype(np.float32)).reshape(n, h, head_dim)
+
+
+def repro_inputs(layer: int):
+    """repro.rs:55-63 for one layer: (k_prior, v_prior, k_new, v_new, q_new)."""
+    base = np.float32(1.0) + np.float32(layer) * np.float32(0.13)
+    sd = lambda c: np.float32(np.float32(c) * base)  # noqa: E731
+    k_prior = repro_mk(sd(0.7), REPRO_PRIOR_LEN, REPRO_N_KV_HEADS)
+    v_prior = repro_mk(sd(1.3), REPRO_PRIOR_LEN, REPRO_N_KV_HEADS)
+    k_new = repro_mk(sd(0.9), 1, REPRO_N_KV_HEADS)
+    v_new = repro_mk(sd(1.7), 1, REPRO_N_KV_HEADS)
+    q_new = repro_mk(sd(2.1), 1, REPRO_N_HEADS)
+    return k_prior, v_prior, k_new, v_new, q_new

@@ -1,0 +1,99 @@
+"""CPU (numpy fp32) restatement of the reference's Qwen3 forward around the
+attention hot path -- the reference's CPU route (candle CPU + the unfused
+varlen attention of layers/attention.rs:85-137).
+
+TEST INFRASTRUCTURE ONLY (the checker and the timed CPU baseline; see
+nvkv_oracle.py).  Layer order follows models/qwen3.rs:126-146 (attention),
+:179-183 (MLP), :226-243 (decoder layer), :285-297 (model), and
+embed_head.rs:89-119 (last-token logits).  fp32 throughout, like config 1.
+Weights come in as a dict of numpy arrays (unsharded), so a test can hand it
+exactly the weights a GPU model uses.
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import numpy as np
+
+import nvkv_oracle as O
+
+
+def _rms(x, w, eps):
+    var = np.mean(x * x, axis=-1, keepdims=True, dtype=np.float32)
+    return (x / np.sqrt(var + np.float32(eps))).astype(np.float32) * w
+
+
+def _silu(x):
+    return x / (np.float32(1.0) + np.exp(-x))
+
+
+class Qwen3CPU:
+    """weights: 'embed' [V,H], 'norm' [H], 'lm_head' [V,H] and per layer i:
+    f'{i}.qkv' [(Hq+2Hkv)D, H], f'{i}.o' [H, HqD], f'{i}.gate_up' [2F, H],
+    f'{i}.down' [H, F], f'{i}.ln1', f'{i}.ln2' [H], f'{i}.qn', f'{i}.kn' [D]."""
+
+    def __init__(self, cfg, weights: Dict[str, np.ndarray], num_blocks: int, block_size: int):
+        self.cfg, self.w = cfg, weights
+        D = cfg.head_dim
+        self.P = block_size
+        shape = (num_blocks, block_size, cfg.num_key_value_heads, D)
+        self.k = [np.zeros(shape, np.float32) for _ in range(cfg.num_hidden_layers)]
+        self.v = [np.zeros(shape, np.float32) for _ in range(cfg.num_hidden_layers)]
+
+    def layer(self, i: int, h, residual, positions, ctx):
+        c, w = self.cfg, self.w
+        Hq, Hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        if residual is None:
+            x, residual = _rms(h, w[f"{i}.ln1"], c.rms_norm_eps), h
+        else:
+            residual = h + residual
+            x = _rms(residual, w[f"{i}.ln1"], c.rms_norm_eps)
+        qkv = x @ w[f"{i}.qkv"].T
+        q, k, v = O.qknorm_rope(qkv, positions, Hq, Hkv, D, w[f"{i}.qn"], w[f"{i}.kn"],
+                                c.rms_norm_eps, c.rope_theta, "f32")
+        o = O.attention_forward(q, k, v, ctx, self.k[i], self.v[i], D ** -0.5, acc=np.float32)
+        a = o.reshape(len(q), -1) @ w[f"{i}.o"].T
+        residual = a + residual
+        x = _rms(residual, w[f"{i}.ln2"], c.rms_norm_eps)
+        gu = x @ w[f"{i}.gate_up"].T
+        F = gu.shape[1] // 2
+        return (_silu(gu[:, :F]) * gu[:, F:]) @ w[f"{i}.down"].T, residual
+
+    def forward(self, input_ids, positions, ctx, layers: int = None) -> np.ndarray:
+        """Returns last-token logits [B, V] (embed_head.rs:96-113)."""
+        c, w = self.cfg, self.w
+        h = w["embed"][input_ids]
+        residual = None
+        for i in range(layers if layers is not None else c.num_hidden_layers):
+            h, residual = self.layer(i, h, residual, positions, ctx)
+        h = _rms(h + residual, w["norm"], c.rms_norm_eps)
+        last = ctx.cu_seqlens_q[1:].astype(np.int64) - 1
+        if len(ctx.seq_need_compute_logits):
+            last = last[ctx.seq_need_compute_logits]
+        return h[last] @ w["lm_head"].T
+
+
+def advance(seqs: List[O.Seq], tokens, free_blocks: List[int], P: int) -> None:
+    """Scheduler::postprocess + BlockManager::may_append (scheduler.rs:53-96,
+    block_manager.rs): append the sampled token and a page when one fills."""
+    for s, t in zip(seqs, tokens):
+        s.num_cached_tokens = s.num_context_tokens()
+        s.token_ids.append(int(t))
+        s.num_new_tokens = 1
+        if (len(s.token_ids) + P - 1) // P > len(s.block_table):
+            s.block_table.append(free_blocks.pop())
+
+
+def greedy_generate(model: Qwen3CPU, seqs: List[O.Seq], steps: int,
+                    free_blocks: List[int]) -> List[List[int]]:
+    """ModelRunner::run with greedy (argmax) sampling, no preemption: one
+    prefill step for every prompt, then `steps - 1` decode steps."""
+    P = model.P
+    out: List[List[int]] = [[] for _ in seqs]
+    for _ in range(steps):
+        ids, pos, ctx = O.prepare_model_input(seqs, P)
+        nxt = np.argmax(model.forward(ids, pos, ctx), axis=-1)
+        for o, t in zip(out, nxt):
+            o.append(int(t))
+        advance(seqs, nxt, free_blocks, P)
+    return out

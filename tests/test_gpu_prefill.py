@@ -1,0 +1,83 @@
+"""Kernel 3 (tcgen05 varlen paged prefill, q_len > 1) vs the oracle, and
+mixed decode + prefill batches (both kernels in one call).
+
+Tolerance (parity gate): max-abs 2e-2, mean-abs 2e-3 vs the fp64 oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+import nvkv
+import nvkv_oracle as O
+from helpers import assert_attention_close, cu, f32, gather_seq, make_paged
+
+pytestmark = pytest.mark.gpu
+
+
+def _contiguous_case(lens, hq, hkv, dtype=torch.bfloat16, causal=True, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    d, T = 128, sum(lens)
+    q = torch.randn(T, hq, d, generator=g).to(dtype).cuda()
+    k = torch.randn(T, hkv, d, generator=g).to(dtype).cuda()
+    v = torch.randn(T, hkv, d, generator=g).to(dtype).cuda()
+    scale = d ** -0.5
+    out = nvkv.paged_attention(q, k, v, cu(lens), cu(lens), None, max(lens), max(lens), scale,
+                               causal=causal)
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == 0
+    c = np.cumsum([0] + lens)
+    for b in range(len(lens)):
+        want = O.causal_attention_one(f32(q)[c[b]:c[b + 1]], f32(k)[c[b]:c[b + 1]],
+                                      f32(v)[c[b]:c[b + 1]], scale, causal)
+        assert_attention_close(out[c[b]:c[b + 1]], want, f"seq {b} len {lens[b]}")
+
+
+@pytest.mark.parametrize("lens", [[2], [128], [129, 3], [127, 300, 1024], [2048]])
+def test_prefill_pure_causal(lens):
+    """No block table: flash_attn_varlen(causal=true) on the fresh K/V."""
+    _contiguous_case(lens, 8, 2, seed=len(lens))
+
+
+@pytest.mark.parametrize("group", [1, 4, 8])
+def test_prefill_gqa_groups(group):
+    _contiguous_case([200, 77], 2 * group, 2, seed=group)
+
+
+def test_prefill_f16_and_noncausal():
+    _contiguous_case([150, 64], 4, 4, dtype=torch.float16, seed=3)
+    _contiguous_case([150, 64], 4, 2, causal=False, seed=5)
+
+
+def _paged_case(q_lens, k_lens, hq, hkv, page=256, seed=0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    d = 128
+    kc, vc, bt, tables = make_paged(k_lens, page, hkv, d,
+                                    sum((L + page - 1) // page for L in k_lens) + 2, g, dtype)
+    T = sum(q_lens)
+    q = torch.randn(T, hq, d, generator=g).to(dtype).cuda()
+    scale = d ** -0.5
+    out = nvkv.paged_attention(q, kc, vc, cu(q_lens), cu(k_lens),
+                               torch.from_numpy(bt.view(np.int32)).cuda(), max(q_lens),
+                               max(k_lens), scale)
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == 0
+    c = np.cumsum([0] + q_lens)
+    for b in range(len(q_lens)):
+        kb, vb = gather_seq(kc, vc, tables[b], k_lens[b])
+        want = O.causal_attention_one(f32(q)[c[b]:c[b + 1]], kb, vb, scale)
+        assert_attention_close(out[c[b]:c[b + 1]], want, f"seq {b} q={q_lens[b]} k={k_lens[b]}")
+
+
+def test_prefill_paged_prefix_cache_hit():
+    """Prefix-cache hit / chunked prefill: k_len > q_len, bottom-right causal."""
+    _paged_case([100, 256, 300], [356, 512, 377], 8, 2, seed=1)
+
+
+def test_mixed_decode_and_prefill_batch():
+    """One step with decode rows (q_len 1) and prefill chunks: the decode
+    kernel and the tcgen05 kernel each take their own sequences."""
+    _paged_case([1, 130, 1, 1, 64, 2], [900, 130, 2, 4000, 600, 258], 16, 8, seed=2)
+
+
+def test_prefill_page_128():
+    _paged_case([200, 5], [600, 133], 4, 1, page=128, seed=6)
