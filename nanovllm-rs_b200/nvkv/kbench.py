@@ -1,0 +1,184 @@
+"""Per-kernel microbenchmarks of the nvkv path (CUDA-event timed).
+
+    python -m nvkv.kbench [--case NAME ...] [--iters N]     (from nanovllm-rs_b200/)
+
+Cases (one JSON line each; bytes/flops are the algorithmic figures):
+  store_cfg2      nvkv_store_kvcache: 64 tokens + 8 padded
+                  slots, 8 kv heads, 2048-block pool                     (HBM)
+  store_prefill   the same at T = 16384 (a full 16384-token prefill step)  (HBM)
+  prologue_8b     nvkv_qknorm_rope + fused store, Qwen3-8B TP1 decode T=256 (HBM)
+  decode_cfg2     nvkv_paged_attention decode, config 2: B=64, 16q/8kv,
+                  L ~ U[512,4096], P=256, 2048-block pool                 (HBM)
+  decode_8b_tp1   one layer of the Qwen3-8B TP1 decode step (B=256, 32q/8kv) (HBM)
+  decode_8b_tp8   the same layer at TP8 per GPU (4q/1kv)                   (HBM)
+  decode_32b_tp8  Qwen3-32B TP8 per GPU: B=64, 8q/1kv, L=32768            (HBM)
+  prefill_8b      tcgen05 prefill, Qwen3-8B TP1: 16 prompts x 1024, causal (tensor)
+Inputs of every HBM case exceed L2 or are rotated through enough copies
+that each timed launch reads cold data.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import numpy as np
+import torch
+
+from . import ops
+
+_ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def _peaks():
+    try:
+        p = json.load(open(os.path.join(_ROOT, "MEASURED_PEAKS.json")))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def _time(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn(0)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(iters)]
+    for i, (a, b) in enumerate(evs):
+        a.record()
+        fn(i)
+        b.record()
+    torch.cuda.synchronize()
+    t = sorted(a.elapsed_time(b) for a, b in evs)
+    return t[len(t) // 2] * 1e-3, t[0] * 1e-3  # median, min (seconds)
+
+
+def _paged(lens, page, hkv, nblocks, seed, copies=1):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    need = [(int(L) + page - 1) // page for L in lens]
+    assert sum(need) <= nblocks
+    perm = rng.permutation(nblocks)
+    bt = np.zeros((len(lens), max(need)), np.int32)
+    u = 0
+    for i, n in enumerate(need):
+        bt[i, :n] = perm[u:u + n]
+        u += n
+    caches = [(torch.randn(nblocks, page, hkv, 128, generator=g, device="cuda",
+                           dtype=torch.bfloat16),
+               torch.randn(nblocks, page, hkv, 128, generator=g, device="cuda",
+                           dtype=torch.bfloat16)) for _ in range(copies)]
+    return caches, torch.from_numpy(bt).cuda()
+
+
+def case_store(T, pad, iters):
+    hkv, page, nb = 8, 256, 2048
+    rng = np.random.default_rng(0)
+    slots = rng.choice(nb * page, T, replace=False).astype(np.int64)
+    slots[rng.choice(T, pad, replace=False)] = -1 if pad else slots[:0]
+    sm = torch.from_numpy(slots).cuda()
+    copies = 8 if T < 4096 else 2
+    srcs = [(torch.randn(T, hkv, 128, device="cuda").bfloat16(),
+             torch.randn(T, hkv, 128, device="cuda").bfloat16()) for _ in range(copies)]
+    kc = torch.zeros(nb, page, hkv, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    fn = lambda i: ops.store_kvcache(srcs[i % copies][0], srcs[i % copies][1], kc, vc, sm)  # noqa
+    med, mn = _time(fn, iters)
+    valid = int((slots >= 0).sum())
+    nbytes = 2 * 2 * valid * hkv * 128 * 2 + 8 * T
+    return dict(kernel="store_kvcache", T=T, valid=valid, bytes=nbytes, s=med, bound="hbm")
+
+
+def case_prologue(T, iters):
+    hq, hkv, page = 32, 8, 256
+    nb = (T + page - 1) // page + 4
+    qkv = [torch.randn(T, (hq + 2 * hkv) * 128, device="cuda").bfloat16() for _ in range(4)]
+    pos = torch.randint(0, 40960, (T,), device="cuda")
+    slots = torch.from_numpy(np.random.default_rng(1).choice(nb * page, T, replace=False)).cuda()
+    w = torch.ones(128, device="cuda", dtype=torch.bfloat16)
+    kc = torch.zeros(nb, page, hkv, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    qo = torch.empty(T, hq, 128, device="cuda", dtype=torch.bfloat16)
+    fn = lambda i: ops.qknorm_rope(qkv[i % 4], pos, hq, hkv, w, w, 1e-6, 1e6, 40960,  # noqa
+                                   k_cache=kc, v_cache=vc, slot_mapping=slots, q_out=qo)
+    med, _ = _time(fn, iters)
+    nbytes = T * (hq + 2 * hkv) * 128 * 2 + T * (hq + 2 * hkv) * 128 * 2 + 2 * 8 * T
+    return dict(kernel="qknorm_rope+store", T=T, bytes=nbytes, s=med, bound="hbm")
+
+
+def case_decode(name, lens, hq, hkv, nblocks, iters, copies=1):
+    page = 256
+    caches, bt = _paged(lens, page, hkv, nblocks, 3, copies)
+    B = len(lens)
+    q = torch.randn(B, hq, 128, device="cuda").bfloat16()
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    cu_k = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).cuda()
+    out = torch.empty_like(q)
+    ws = torch.empty(max(16, ops.workspace_size(B, hq, hkv, 1, int(max(lens)))),
+                     dtype=torch.uint8, device="cuda")
+    fn = lambda i: ops.paged_attention(q, caches[i % copies][0], caches[i % copies][1],  # noqa
+                                       cu_q, cu_k, bt, 1, int(max(lens)), 128 ** -0.5, out=out,
+                                       workspace=ws)
+    med, _ = _time(fn, iters)
+    nblk = sum((int(L) + page - 1) // page for L in lens)
+    nbytes = int(np.sum(lens)) * hkv * 128 * 2 * 2 + 2 * B * hq * 128 * 2 + 4 * nblk + 8 * (B + 1)
+    return dict(kernel=name, B=B, hq=hq, hkv=hkv, L_mean=float(np.mean(lens)), bytes=nbytes, s=med,
+                splits=bool(ops.workspace_size(B, hq, hkv, 1, int(max(lens)))), bound="hbm")
+
+
+def case_prefill(iters, nseq=16, L=1024, hq=32, hkv=8):
+    page = 256
+    lens = [L] * nseq
+    caches, bt = _paged(lens, page, hkv, nseq * L // page + 2, 5)
+    T = nseq * L
+    q = torch.randn(T, hq, 128, device="cuda").bfloat16()
+    cu = torch.from_numpy(np.arange(0, T + 1, L).astype(np.int32)).cuda()
+    out = torch.empty_like(q)
+    fn = lambda i: ops.paged_attention(q, caches[0][0], caches[0][1], cu, cu, bt, L, L,  # noqa
+                                       128 ** -0.5, out=out)
+    med, _ = _time(fn, iters)
+    pairs = nseq * L * (L + 1) // 2
+    return dict(kernel="prefill_tcgen05", nseq=nseq, L=L, hq=hq, hkv=hkv,
+                flops=4 * 128 * hq * pairs, s=med, bound="tensor")
+
+
+CASES = {
+    "store_cfg2": lambda it: case_store(72, 8, it),
+    "store_prefill": lambda it: case_store(16384, 0, it),
+    "prologue_8b": lambda it: case_prologue(256, it),
+    "decode_cfg2": lambda it: case_decode(
+        "decode_cfg2", np.random.default_rng(2).integers(512, 4097, 64), 16, 8, 2048, it, 4),
+    "decode_8b_tp1": lambda it: case_decode(
+        "decode_8b_tp1", np.random.default_rng(4).integers(1025, 1537, 256), 32, 8, 1560, it, 2),
+    "decode_8b_tp8": lambda it: case_decode(
+        "decode_8b_tp8", np.random.default_rng(4).integers(1025, 1537, 256), 4, 1, 1560, it, 8),
+    "decode_32b_tp8": lambda it: case_decode(
+        "decode_32b_tp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
+    "prefill_8b": lambda it: case_prefill(it),
+}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", nargs="*", default=list(CASES))
+    ap.add_argument("--iters", type=int, default=50)
+    a = ap.parse_args(argv)
+    hbm, tf, src = _peaks()
+    for name in a.case:
+        r = CASES[name](a.iters)
+        if r["bound"] == "hbm":
+            ach = r["bytes"] / r["s"] / 1e9
+            r.update(case=name, us=round(r["s"] * 1e6, 2), achieved_gbs=round(ach, 1),
+                     peak_gbs=hbm, frac=round(ach / hbm, 4), peak_source=src)
+        else:
+            ach = r["flops"] / r["s"] / 1e12
+            r.update(case=name, us=round(r["s"] * 1e6, 2), achieved_tflops=round(ach, 1),
+                     peak_tflops=tf, frac=round(ach / tf, 4), peak_source=src)
+        r.pop("s")
+        print(json.dumps(r), flush=True)
+    from ._lib import device_error
+    assert device_error() == 0
+
+
+if __name__ == "__main__":
+    main()
