@@ -226,11 +226,13 @@ def run_nvkv(a):
         sampler.start()
         time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("bench_timed")  # ncu --nvtx-include "bench_timed/"
     e0.record()
     for _ in range(a.steps):
         run()
     e1.record()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     clocks = sampler.stop() if sampler else None
     ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
     _barrier(world)

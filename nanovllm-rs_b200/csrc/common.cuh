@@ -3,7 +3,7 @@
 // * host-side status/error plumbing behind the C ABI (thread-local message);
 // * the device error word that bounds checks write instead of faulting;
 // * thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor, no
-//   multicast anywhere in this library), ldmatrix and mma.sync;
+//   cluster-wide variants anywhere in this library), ldmatrix and mma.sync;
 // * tensor-map encoding through the driver entry point (no -lcuda needed).
 #pragma once
 
@@ -170,7 +170,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
-// ---- TMA (no multicast) ------------------------------------------------------
+// ---- TMA (single-CTA destination only) ------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -8,7 +8,7 @@
 // One CTA = 128 query rows of one query head of one sequence.  6 warps:
 //   warp 0      TMA producer: Q tile once, then K/V tiles of 128 keys
 //               (pages resolved through block_tables) into a 2-stage ring,
-//               SWIZZLE_128B, no multicast;
+//               SWIZZLE_128B, each CTA loading its own tiles;
 //   warp 1      allocates 512 TMEM columns and issues every tcgen05.mma from
 //               one thread: S_j = Q.K_j^T (K-major A and B, M=N=128, K=16 x 8)
 //               into a double-buffered S in TMEM, then O_j = P_j.V_j (P K-major

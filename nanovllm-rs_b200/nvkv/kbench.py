@@ -39,18 +39,28 @@ def _peaks():
 
 
 def _time(fn, iters, warmup=3):
-    for _ in range(warmup):
-        fn(0)
+    """Mean device time per launch: `iters` launches are captured into one
+    CUDA graph and the replay is timed with two CUDA events, so no host
+    overhead sits between launches (what a graph-captured decode step sees)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn(0)
+    torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(iters)]
-    for i, (a, b) in enumerate(evs):
-        a.record()
-        fn(i)
-        b.record()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
     torch.cuda.synchronize()
-    t = sorted(a.elapsed_time(b) for a, b in evs)
-    return t[len(t) // 2] * 1e-3, t[0] * 1e-3  # median, min (seconds)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e-3 / iters, None
 
 
 def _paged(lens, page, hkv, nblocks, seed, copies=1):
@@ -134,8 +144,10 @@ def case_prefill(iters, nseq=16, L=1024, hq=32, hkv=8):
     q = torch.randn(T, hq, 128, device="cuda").bfloat16()
     cu = torch.from_numpy(np.arange(0, T + 1, L).astype(np.int32)).cuda()
     out = torch.empty_like(q)
+    ws = torch.empty(max(16, ops.workspace_size(nseq, hq, hkv, L, L)), dtype=torch.uint8,
+                     device="cuda")
     fn = lambda i: ops.paged_attention(q, caches[0][0], caches[0][1], cu, cu, bt, L, L,  # noqa
-                                       128 ** -0.5, out=out)
+                                       128 ** -0.5, out=out, workspace=ws)
     med, _ = _time(fn, iters)
     pairs = nseq * L * (L + 1) // 2
     return dict(kernel="prefill_tcgen05", nseq=nseq, L=L, hq=hq, hkv=hkv,

@@ -33,8 +33,9 @@ def _rope_close(got, want, x_normed, pos, dtype, head_dim=128, theta=1e6):
     moves freq = pos * inv_freq by up to freq * 2^-23, and a cos/sin value can
     then round to the neighbouring dtype value, so element i of the rotated
     pair (x1, x2) may differ by (|x1| + |x2|) * (ulp + 4 * freq_i * 2^-23) plus
-    one output ulp.  At most 5 % of elements may differ at all (numpy's f32
-    exp/cos already differ from correctly rounded ones on ~1.4 %) and the mean
+    one output ulp.  At most 5 % (bf16) / 20 % (f16) of elements may differ at
+    all (numpy's f32 exp/cos already differ from correctly rounded ones on
+    ~1.4 % of bf16 outputs; f16 keeps 3 more bits, so ~8x as many flip) and the mean
     absolute difference stays inside the parity bound (2e-3)."""
     half = head_dim // 2
     freq = pos.astype(np.float64)[:, None] * O.rope_inv_freq(head_dim, theta)[None, :]
@@ -45,7 +46,8 @@ def _rope_close(got, want, x_normed, pos, dtype, head_dim=128, theta=1e6):
     tol = mag * (u + 4 * freq * 2.0 ** -23) + u * np.maximum(1.0, np.abs(want)) + 1e-12
     d = np.abs(got - want)
     assert (d <= tol).all(), f"{(d > tol).sum()} elements beyond the bound, worst {d.max()}"
-    assert np.mean(d > 0) <= 5e-2, f"{np.mean(d > 0):.2e} of elements differ"
+    cap = 5e-2 if dtype == "bf16" else 2e-1  # f16 keeps 3 more bits: ~8x the flips
+    assert np.mean(d > 0) <= cap, f"{np.mean(d > 0):.2e} of elements differ"
     assert d.mean() <= 2e-3
 
 
