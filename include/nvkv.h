@@ -158,6 +158,32 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
                          nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * nvkv_paged_attention without a workspace argument, for callers that cannot
+ * allocate device memory on the call path (an engine that has handed nearly
+ * all free GPU memory to its KV pool, code inside a stream capture that may
+ * not allocate, a binding with no allocator at hand).  No counterpart in the
+ * reference: its flash-attn call allocates through candle.
+ * Same inputs, outputs and validation as nvkv_paged_attention.  The split-KV
+ * scratch is a file-scope device array of NVKV_NOALLOC_SCRATCH_BYTES held by
+ * every GPU that loads the library until exit; batches whose plan needs more
+ * are rejected with NVKV_ERR_WORKSPACE.  All calls share that array (it keeps
+ * the last call's contents; nothing needs to start zeroed), so calls that
+ * overlap on the GPU race: serialise them.  The first call on a device looks
+ * the array's address up once; make it before any stream capture.  Calls no
+ * cudaMalloc/cudaFree.
+ * ---------------------------------------------------------------------- */
+#define NVKV_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+int nvkv_paged_attention_noalloc(const void* q, int64_t q_stride, int64_t num_q_tokens,
+                                 const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                 int64_t kv_stride, void* out, const uint32_t* cu_seqlens_q,
+                                 const uint32_t* cu_seqlens_k, const uint32_t* block_tables,
+                                 int64_t block_table_stride, int num_seqs, int max_seqlen_q,
+                                 int max_seqlen_k, int num_q_heads, int num_kv_heads,
+                                 int head_dim, int page_size, float softmax_scale, int causal,
+                                 int dtype, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Host-side mirror of the reference's operator surface, for callers that
  * drive the path the way nanovllm_rs's Attention does: a per-thread Context
  * (utils/context.rs:4-54) published once per step, and an Attention object

@@ -48,6 +48,9 @@ SIGNATURES = {
                                             ctypes.POINTER(_sz)],
     "nvkv_paged_attention": [_p, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _i32,
                              _i32, _i32, _i32, _i32, _i32, _f32, _i32, _p, _sz, _i32, _p],
+    "nvkv_paged_attention_noalloc": [_p, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64,
+                                     _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
+                                     _p],
     "nvkv_context_set": [_p, _p, _i32, _i32, _i32, _p, _i64, _p, _p, _i64],
     "nvkv_context_reset": [],
     "nvkv_attention_create": [_f32, ctypes.POINTER(_p)],
