@@ -82,6 +82,13 @@ def decode_bytes(w, hq, hkv, D=128):
     return kv + qo + meta
 
 
+# DRAM bytes per algorithmic byte of the decode attention kernel, from one
+# ncu capture of the identical per-layer shape (B=256, 32q/8kv, ctx
+# U[1025,1536]; profiles/paged_decode_qwen3-8b-tp1-layer.md):
+# (1,386,555,000 read + 7,612,672 written) / 1,355,329,068 algorithmic.
+DECODE_DRAM_PER_ALG_BYTE = (1386555000 + 7612672) / 1355329068
+
+
 def load_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -298,7 +305,9 @@ def run_nvkv(a):
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "bytes_per_launch": int(nbytes), "us_per_launch": round(kern_ms * 1e3, 2),
-                         "traffic": None},
+                         "traffic": int(nbytes * DECODE_DRAM_PER_ALG_BYTE),
+                         "traffic_source": "ncu dram__bytes_read+write of the same per-layer "
+                                           "shape, scaled to this launch's algorithmic bytes"},
             "clocks": clocks,
         }
         if world == 1:

@@ -184,6 +184,30 @@ int nvkv_paged_attention_noalloc(const void* q, int64_t q_stride, int64_t num_q_
                                  int dtype, nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Fused epilogues around the path (one launch each instead of candle's op
+ * chains), at the reference's rounding points.
+ *
+ * nvkv_rms_norm replaces nanovllm_rs/src/layers/layernorm.rs:18-25
+ * (RMSNorm::forward, residual == NULL) and :27-42 (residual_forward):
+ *   s = x (+ residual) in f32; residual <- dtype(s) when given (in place);
+ *   out = dtype(dtype(s * 1/sqrt(mean(s^2) + eps)) * weight)
+ * x/residual/out: [num_tokens, hidden] rows with the given strides
+ * (elements); weight [hidden].  hidden % 8 == 0, hidden <= 8192, rows 16-byte
+ * aligned.
+ *
+ * nvkv_silu_and_mul replaces layers/activation.rs:5-17 (SiluAndMul):
+ *   out[t, i] = dtype(dtype(silu(g)) * u), g = gate_up[t, i],
+ *   u = gate_up[t, inter + i]; gate_up [num_tokens, 2*inter], out
+ *   [num_tokens, inter].  inter % 8 == 0.
+ * ---------------------------------------------------------------------- */
+int nvkv_rms_norm(const void* x, int64_t x_stride, void* residual, int64_t residual_stride,
+                  const void* weight, float eps, void* out, int64_t out_stride,
+                  int64_t num_tokens, int hidden, int dtype, nvkv_stream_t stream);
+
+int nvkv_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
+                      int64_t num_tokens, int inter, int dtype, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Host-side mirror of the reference's operator surface, for callers that
  * drive the path the way nanovllm_rs's Attention does: a per-thread Context
  * (utils/context.rs:4-54) published once per step, and an Attention object

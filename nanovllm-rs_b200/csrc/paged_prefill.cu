@@ -5,22 +5,31 @@
 // layers/attention.rs:43-73; FA2 with SM80 mma.sync) for every sequence
 // whose q_len > 1 (q_len == 1 rows run on the decode kernel).
 //
-// One CTA = 128 query rows of one query head of one sequence.  6 warps:
-//   warp 0      TMA producer: Q tile once, then K/V tiles of 128 keys
-//               (pages resolved through block_tables) into a 2-stage ring,
+// One CTA = 128 query rows x TWO query heads of the same kv group (slots A
+// and B; one slot when the group size is odd).  Both slots read the same K/V
+// tiles, so every K/V tile is fetched once per head pair, and the two
+// softmax warpgroups ping-pong against the tensor core.  10 warps:
+//   warp 0      TMA producer: Q_A/Q_B once, then K_j, V_j (128 keys each,
+//               pages resolved through block_tables) through a 3-slot ring,
 //               SWIZZLE_128B, each CTA loading its own tiles;
-//   warp 1      allocates 512 TMEM columns and issues every tcgen05.mma from
-//               one thread: S_j = Q.K_j^T (K-major A and B, M=N=128, K=16 x 8)
-//               into a double-buffered S in TMEM, then O_j = P_j.V_j (P K-major
-//               from shared memory, V MN-major) into a TMEM O tile;
-//               tcgen05.commit signals the mbarriers;
-//   warps 2-5   softmax warpgroup: thread r owns query row r (TMEM lane r).
-//               Per key tile it reads its S row from TMEM (tcgen05.ld
-//               32x32b), applies the causal / length mask (bottom-right
-//               aligned: key j visible to query i iff j <= i + k_len - q_len),
-//               runs the fp32 online softmax, writes P (bf16/f16) into the
-//               swizzled shared-memory tile the next MMA reads, and folds the
-//               previous O tile into a 128-float register accumulator.
+//   warp 1      allocates all 512 TMEM columns (S_A, S_B, O_A, O_B) and
+//               issues every tcgen05.mma.cta_group::1.kind::f16 from one
+//               thread in the order  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1),
+//               so the tensor core computes one slot while the other slot's
+//               softmax runs; tcgen05.commit arrives on the mbarriers;
+//   warps 2-5   softmax warpgroup of slot A, warps 6-9 of slot B: thread r
+//               owns query row r (TMEM lane r).  Per key tile it reads its S
+//               row from TMEM in two passes of 64 columns (tcgen05.ld 32x32b;
+//               max first, then exponentials), masks (causal, bottom-right:
+//               key j visible to query i iff j <= i + k_len - q_len), takes
+//               the row max, and rescales the TMEM O row (tcgen05.ld/st) only
+//               when the max grew by more than 2^8 -- otherwise it keeps the
+//               stale max, whose exponentials stay <= 256 and exact enough in
+//               fp32/bf16 -- then writes P = 2^(s*scale - m) into a swizzled
+//               K-major shared-memory tile.  Half of the exponentials use the
+//               MUFU ex2 unit, half a degree-3 polynomial on the FMA pipe.
+//   O accumulates in TMEM across key tiles (PV MMAs chain with
+//   accumulate = 1); the epilogue divides by the row sum and stores bf16/f16.
 // Roofline: tensor cores; flops = 4 * D * (visible (query, key) pairs).
 #include <type_traits>
 
@@ -31,19 +40,22 @@ namespace nvkv {
 constexpr int kPfD = 128;
 constexpr int kPfBM = 128;
 constexpr int kPfBN = 128;
-constexpr int kPfStages = 2;
-constexpr int kPfThreads = 6 * 32;
+constexpr int kPfSlots = 3;                 // K/V ring: K_j and V_j each take one slot
+constexpr int kPfThreads = 10 * 32;
 constexpr int kPfHalf = 128 * 128;          // 128 rows x 128 B (64 elements)
 constexpr int kPfTile = 2 * kPfHalf;        // 32 KB: 128 rows x 128 elements
-constexpr int kPfOffQ = 0;
-constexpr int kPfOffK = kPfOffQ + kPfTile;
-constexpr int kPfOffV = kPfOffK + kPfStages * kPfTile;
-constexpr int kPfOffP = kPfOffV + kPfStages * kPfTile;
-constexpr int kPfOffBar = kPfOffP + kPfTile;
-constexpr int kPfNumBars = 1 + 3 * kPfStages + 2 + 2 + 1 + 1;
+constexpr int kPfOffQA = 0;
+constexpr int kPfOffQB = kPfOffQA + kPfTile;
+constexpr int kPfOffKV = kPfOffQB + kPfTile;
+constexpr int kPfOffPA = kPfOffKV + kPfSlots * kPfTile;
+constexpr int kPfOffPB = kPfOffPA + kPfTile;
+constexpr int kPfOffBar = kPfOffPB + kPfTile;
+constexpr int kPfNumBars = 1 + 2 * kPfSlots + 8;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
-constexpr uint32_t kPfColS0 = 0, kPfColS1 = 128, kPfColO = 256;
+constexpr float kPfRescaleLog2 = 8.0f;  // rescale O only when the max grows by > 2^8
+
+static_assert(kPfSmemBytes <= 232448, "prefill shared memory exceeds 227 KB");
 
 struct PrefillParams {
   void* out;
@@ -54,6 +66,7 @@ struct PrefillParams {
   int64_t num_blocks;
   int num_q_heads;
   int group;
+  int pair;  // 1: slots A/B are heads 2p, 2p+1 of one kv group; 0: slot A only
   int page_size;
   int num_q_tiles;
   int causal;
@@ -102,18 +115,82 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+#define NVKV_R32(r)                                                                          \
+  "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),    \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),      \
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),    \
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),    \
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+#define NVKV_W32(r)                                                                          \
+  "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),        \
+      "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), \
+      "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),          \
+      "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),          \
+      "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+#define NVKV_REGLIST                                                                           \
+  "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24," \
+  "%25,%26,%27,%28,%29,%30,%31}"
+#define NVKV_REGLIST1                                                                          \
+  "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24," \
+  "%25,%26,%27,%28,%29,%30,%31,%32}"
 // 32 consecutive fp32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 " NVKV_REGLIST ", [%32];"
+               : NVKV_W32(r)
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], " NVKV_REGLIST1 ";" ::"r"(taddr),
+               NVKV_R32(r)
+               : "memory");
+}
+
+// 16 consecutive fp32 columns (used where the 128 S values are still live)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// 2^x on the MUFU unit (PTX ex2.approx).
+__device__ __forceinline__ float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2];
+// 2^f by a degree-3 polynomial fitted here to the exact function (max
+// relative error 7.5e-5, far below bf16's 2^-9 half-ulp); 2^n is added into
+// the exponent bits.  Valid for x in [-125, 126]; smaller x is clamped (the
+// result, ~2^-125, is negligible next to the row sum it joins).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: t's low mantissa bits hold round(x)
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(0.05517153f, f, 0.24261111f);
+  p = fmaf(p, f, 0.69326103f);
+  p = fmaf(p, f, 0.99992806f);
+  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 // Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bit.
@@ -127,6 +204,81 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, uint32_t b_mn
          ((uint32_t)(kPfBN >> 3) << 17) | ((uint32_t)(kPfBM >> 4) << 24);
 }
 
+// Two P values -> one packed 16-bit pair.  bf16: round-half-up on the integer
+// bits and a byte permute (ALU pipe) instead of a conversion instruction (XU
+// pipe, the softmax bottleneck); P >= 0 and finite, and exact ties (the only
+// inputs where this differs from round-to-nearest-even) occur with
+// probability 2^-16.  f16 keeps the conversion instruction.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_p(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack_p<__nv_bfloat16>(float a, float b) {
+  return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_p<__half>(float a, float b) {
+  return DT<__half>::from_f2(a, b);
+}
+
+// P for one 64-key half of a row: e = 2^(s*scale - m) (masked keys -> 0),
+// a quarter on the MUFU unit and the rest on the FMA pipe, packed into the
+// swizzled K-major tile; returns the sum of the e values and folds the
+// half's max of s into `mx`.
+template <typename T, bool kMask>
+__device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim, float scale_log2,
+                                             float m_use, uint8_t* half, uint32_t row,
+                                             float& mx) {
+  float rs = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const int i = u * 8 + e;
+      float s0 = sv[i], s1 = sv[i + 1];
+      if (kMask) {
+        s0 = kbase + i <= lim ? s0 : -INFINITY;
+        s1 = kbase + i + 1 <= lim ? s1 : -INFINITY;
+      }
+      mx = fmaxf(mx, fmaxf(s0, s1));
+      const float x0 = fmaf(s0, scale_log2, -m_use), x1 = fmaf(s1, scale_log2, -m_use);
+      float e0 = (e == 0) ? ex2_mufu(x0) : ex2_poly(x0);
+      float e1 = ex2_poly(x1);
+      if (kMask) {
+        e0 = kbase + i <= lim ? e0 : 0.f;
+        e1 = kbase + i + 1 <= lim ? e1 : 0.f;
+      }
+      rs += e0 + e1;
+      pk[e >> 1] = pack_p<T>(e0, e1);
+    }
+    *reinterpret_cast<uint4*>(half + sw128_offset(row, (uint32_t)u)) =
+        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+  return rs;
+}
+
+// S_x = Q_x . K^T over D = 128: 8 MMAs of K = 16, advancing 32 bytes inside
+// the 128-byte swizzle atom (both operands K-major, SWIZZLE_128B).
+__device__ __forceinline__ void pf_issue_s(uint32_t d_tmem, uint32_t sq, uint32_t sk,
+                                           uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < kPfD / 16; ++kk) {
+    const uint32_t o = (kk >> 2) * kPfHalf + (kk & 3) * 32;
+    tc_mma(d_tmem, sdesc(sq + o, 16, 1024), sdesc(sk + o, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+// O_x (+)= P_x . V over 128 keys: P K-major (keys in 64-key halves), V MN-major
+// (D contiguous, the two 64-wide D halves kPfHalf apart = LBO, 8 keys = SBO).
+__device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t sp, uint32_t sv,
+                                            uint32_t idesc, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < kPfBN / 16; ++kk) {
+    const uint64_t ad = sdesc(sp + (kk >> 2) * kPfHalf + (kk & 3) * 32, 16, 1024);
+    const uint64_t bd = sdesc(sv + kk * 16 * 128, kPfHalf, 1024);
+    tc_mma(d_tmem, ad, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kPfThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -137,18 +289,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPfOffBar);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + kPfStages;
-  uint64_t* kv_empty = v_full + kPfStages;
-  uint64_t* s_full = kv_empty + kPfStages;  // [2]
-  uint64_t* s_free = s_full + 2;            // [2]
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_full = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+  uint64_t* kv_full = bars + 1;             // [kPfSlots]
+  uint64_t* kv_empty = kv_full + kPfSlots;  // [kPfSlots]
+  uint64_t* s_full = kv_empty + kPfSlots;   // [2]: S_x written by the MMA
+  uint64_t* s_free = s_full + 2;            // [2]: S_x read by its softmax warpgroup
+  uint64_t* p_full = s_free + 2;            // [2]: P_x written (and O_x rescaled)
+  uint64_t* o_done = p_full + 2;            // [2]: PV_x finished (O_x stable, P_x free)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int qt = p.num_q_tiles - 1 - (int)blockIdx.x;  // heaviest causal tiles first
-  const int hq = blockIdx.y, b = blockIdx.z;
+  const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nslot = p.pair ? 2 : 1;
+  const int head0 = p.pair ? 2 * (int)blockIdx.y : (int)blockIdx.y;
+  const int kvh = head0 / p.group;
 
   const uint32_t qs = p.cu_q[b];
   const int q_len = (int)(p.cu_q[b + 1] - qs);
@@ -165,21 +319,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int last_row = min(i0 + kPfBM, q_len) - 1;
   const int kmax = p.causal ? min(k_len, last_row + off + 1) : k_len;
   const int ntiles = (kmax + kPfBN - 1) / kPfBN;
-  const int kvh = hq / p.group;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
+    for (int s = 0; s < kPfSlots; ++s) {
+      mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&s_free[x], 128);
+      mbar_init(&p_full[x], 128);
+      mbar_init(&o_done[x], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -197,13 +349,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
-      mbar_arrive_expect_tx(q_full, kPfTile);
-      tma_load_3d(smem + kPfOffQ, &tmap_q, q_full, 0, hq, (int)(qs + i0));
-      tma_load_3d(smem + kPfOffQ + kPfHalf, &tmap_q, q_full, 64, hq, (int)(qs + i0));
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % kPfStages;
-        const uint32_t ph = (uint32_t)(j / kPfStages) & 1u;
-        if (j >= kPfStages && !mbar_wait(&kv_empty[st], ph ^ 1u, p.err)) break;
+      mbar_arrive_expect_tx(q_full, nslot * kPfTile);
+      for (int x = 0; x < nslot; ++x) {
+        uint8_t* qd = smem + (x ? kPfOffQB : kPfOffQA);
+        tma_load_3d(qd, &tmap_q, q_full, 0, head0 + x, (int)(qs + i0));
+        tma_load_3d(qd + kPfHalf, &tmap_q, q_full, 64, head0 + x, (int)(qs + i0));
+      }
+      for (int t = 0; t < 2 * ntiles; ++t) {  // K_0, V_0, K_1, V_1, ...
+        const int j = t >> 1;
+        const int s = t % kPfSlots;
+        const uint32_t ph = (uint32_t)(t / kPfSlots) & 1u;
+        if (t >= kPfSlots && !mbar_wait(&kv_empty[s], ph ^ 1u, p.err)) break;
         const int j0 = j * kPfBN;
         int64_t row;
         if (p.block_tables) {
@@ -216,14 +372,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         } else {
           row = (int64_t)ks + j0;
         }
-        uint8_t* kd = smem + kPfOffK + st * kPfTile;
-        uint8_t* vd = smem + kPfOffV + st * kPfTile;
-        mbar_arrive_expect_tx(&k_full[st], kPfTile);
-        tma_load_3d(kd, &tmap_k, &k_full[st], 0, kvh, (int)row);
-        tma_load_3d(kd + kPfHalf, &tmap_k, &k_full[st], 64, kvh, (int)row);
-        mbar_arrive_expect_tx(&v_full[st], kPfTile);
-        tma_load_3d(vd, &tmap_v, &v_full[st], 0, kvh, (int)row);
-        tma_load_3d(vd + kPfHalf, &tmap_v, &v_full[st], 64, kvh, (int)row);
+        uint8_t* dst = smem + kPfOffKV + s * kPfTile;
+        const CUtensorMap* map = (t & 1) ? &tmap_v : &tmap_k;
+        mbar_arrive_expect_tx(&kv_full[s], kPfTile);
+        tma_load_3d(dst, map, &kv_full[s], 0, kvh, (int)row);
+        tma_load_3d(dst + kPfHalf, map, &kv_full[s], 64, kvh, (int)row);
       }
     }
   } else if (warp == 1) {
@@ -232,158 +385,184 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_qk = make_idesc(fmt, 0u);
       constexpr uint32_t idesc_pv = make_idesc(fmt, 1u);
-      const uint32_t sq = smem_u32(smem + kPfOffQ);
-      const uint32_t sp = smem_u32(smem + kPfOffP);
-      bool ok = mbar_wait(q_full, 0, p.err);
-      auto issue_pv = [&](int j) {
-        const int st = j % kPfStages;
-        if (!mbar_wait(p_full, (uint32_t)j & 1u, p.err)) return false;
-        if (!mbar_wait(&v_full[st], (uint32_t)(j / kPfStages) & 1u, p.err)) return false;
+      const uint32_t kv0 = smem_u32(smem + kPfOffKV);
+      const uint32_t sqa = smem_u32(smem + kPfOffQA), sqb = smem_u32(smem + kPfOffQB);
+      const uint32_t spa = smem_u32(smem + kPfOffPA), spb = smem_u32(smem + kPfOffPB);
+#define PF_SLOT(t) (kv0 + (uint32_t)((t) % kPfSlots) * kPfTile)
+#define PF_PAR(t) ((uint32_t)((t) / kPfSlots) & 1u)
+#define PF_FULL(t) (&kv_full[(t) % kPfSlots])
+      bool ok = mbar_wait(q_full, 0, p.err) && mbar_wait(PF_FULL(0), PF_PAR(0), p.err);
+      if (ok) {
         tc_fence_after();
-        const uint32_t sv = smem_u32(smem + kPfOffV + st * kPfTile);
-#pragma unroll
-        for (int kk = 0; kk < kPfBN / 16; ++kk) {
-          // A = P (K-major over keys): half kk/4, +32 B per 16 keys inside the half
-          const uint64_t ad = sdesc(sp + (kk >> 2) * kPfHalf + (kk & 3) * 32, 16, 1024);
-          // B = V (MN-major over D): 16 keys = 16 rows of 128 B; D halves LBO apart
-          const uint64_t bd = sdesc(sv + kk * 16 * 128, kPfHalf, 1024);
-          tc_mma(tmem + kPfColO, ad, bd, idesc_pv, kk > 0 ? 1u : 0u);
+        pf_issue_s(tmem + 0u, sqa, PF_SLOT(0), idesc_qk);
+        tc_commit(&s_full[0]);
+        if (p.pair) {
+          pf_issue_s(tmem + 128u, sqb, PF_SLOT(0), idesc_qk);
+          tc_commit(&s_full[1]);
         }
-        tc_commit(o_full);
-        tc_commit(&kv_empty[st]);
-        return true;
-      };
+        tc_commit(&kv_empty[0]);
+      }
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % kPfStages;
-        const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], (uint32_t)(j / kPfStages) & 1u, p.err)) break;
-        if (j >= 2 && !mbar_wait(&s_free[sb], ((uint32_t)(j >> 1) & 1u) ^ 1u, p.err)) break;
+        const uint32_t pj = (uint32_t)j & 1u;
+        const bool more = j + 1 < ntiles;
+        const int tv = 2 * j + 1, tk = 2 * j + 2;  // V_j and K_{j+1} in the load order
+        ok = mbar_wait(PF_FULL(tv), PF_PAR(tv), p.err) && mbar_wait(&p_full[0], pj, p.err);
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t sk = smem_u32(smem + kPfOffK + st * kPfTile);
-        const uint32_t dcol = sb ? kPfColS1 : kPfColS0;
-#pragma unroll
-        for (int kk = 0; kk < kPfD / 16; ++kk) {
-          const uint32_t o = (kk >> 2) * kPfHalf + (kk & 3) * 32;
-          tc_mma(tmem + dcol, sdesc(sq + o, 16, 1024), sdesc(sk + o, 16, 1024), idesc_qk,
-                 kk > 0 ? 1u : 0u);
+        pf_issue_pv(tmem + 256u, spa, PF_SLOT(tv), idesc_pv, j > 0);
+        tc_commit(&o_done[0]);
+        if (more) {
+          ok = mbar_wait(PF_FULL(tk), PF_PAR(tk), p.err) && mbar_wait(&s_free[0], pj, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          pf_issue_s(tmem + 0u, sqa, PF_SLOT(tk), idesc_qk);
+          tc_commit(&s_full[0]);
         }
-        tc_commit(&s_full[sb]);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
+        if (p.pair) {
+          if (!mbar_wait(&p_full[1], pj, p.err)) break;
+          tc_fence_after();
+          pf_issue_pv(tmem + 384u, spb, PF_SLOT(tv), idesc_pv, j > 0);
+          tc_commit(&o_done[1]);
+        }
+        tc_commit(&kv_empty[tv % kPfSlots]);  // V_j: both P.V issued
+        if (more) {
+          if (p.pair) {
+            if (!mbar_wait(&s_free[1], pj, p.err)) break;
+            tc_fence_after();
+            pf_issue_s(tmem + 128u, sqb, PF_SLOT(tk), idesc_qk);
+            tc_commit(&s_full[1]);
+          }
+          tc_commit(&kv_empty[tk % kPfSlots]);  // K_{j+1}: both S issued
         }
       }
-      if (ok && ntiles > 0) issue_pv(ntiles - 1);
+#undef PF_SLOT
+#undef PF_PAR
+#undef PF_FULL
     }
   } else {
-    // ------------------------------ softmax warpgroup ------------------------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = quarter * 32 + lane;
-    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int qi = i0 + r;
-    const int lim_row = p.causal ? min(k_len - 1, qi + off) : k_len - 1;
-    uint8_t* pbase = smem + kPfOffP;
-
-    float acc[kPfD];
-#pragma unroll
-    for (int d = 0; d < kPfD; ++d) acc[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    bool alive = true;
-
-    for (int j = 0; j < ntiles && alive; ++j) {
-      const int sb = j & 1;
-      // decisions stay warp-uniform: tcgen05.ld below is .sync.aligned
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, p.err))) {
-        alive = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t scol = lane_addr + (sb ? kPfColS1 : kPfColS0);
-      const int lim = lim_row - j * kPfBN;  // visible keys of this tile: c <= lim
-      // pass 1: row max
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(scol + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (c * 32 + i) <= lim ? v[i] : -INFINITY);
-      }
-      const float m_new = fmaxf(m, mx * p.scale_log2);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m - m_use);
-      // fold the previous O tile (its MMA also released the P buffer)
-      if (j >= 1) {
-        if (!__all_sync(0xffffffffu, mbar_wait(o_full, (uint32_t)(j - 1) & 1u, p.err))) {
+    // ------------------------------ softmax warpgroups ------------------------------
+    const int x = (warp - 2) >> 2;  // slot: warps 2-5 -> A, 6-9 -> B
+    if (x < nslot) {
+      const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+      const int r = quarter * 32 + lane;
+      const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t col_s = x ? 128u : 0u, col_o = x ? 384u : 256u;
+      const int qi = i0 + r;
+      const int lim_row = p.causal ? min(k_len - 1, qi + off) : k_len - 1;
+      uint8_t* ptile = smem + (x ? kPfOffPB : kPfOffPA);
+      float m_ref = -INFINITY, l = 0.f;
+      bool alive = true;
+      for (int j = 0; j < ntiles; ++j) {
+        const uint32_t pj = (uint32_t)j & 1u;
+        // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], pj, p.err))) {
           alive = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(lane_addr + kPfColO + c * 32, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = acc[c * 32 + i] * alpha_prev + v[i];
+        const int lim = lim_row - j * kPfBN;  // keys c <= lim are visible
+        // the whole warp sees every key of this tile: no masking needed
+        const bool vis = __all_sync(0xffffffffu, lim >= kPfBN - 1);
+        if (j >= 1) {  // PV_x(j-1) done: O_x is stable and the P_x tile is free
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[x], pj ^ 1u, p.err))) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
         }
+        float rs = 0.f, mx = -INFINITY;
+        bool redo = (j == 0);
+        if (!redo) {
+          // one pass with the current reference max m_ref (exponentials <= 2^8
+          // unless the row max jumped, which the check below catches)
+          const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float sv[64];
+            tmem_ld32(lane_addr + col_s + h * 64, sv);
+            tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
+            tmem_wait_ld();
+            rs += vis ? pf_exp_half<T, false>(sv, h * 64, lim, p.scale_log2, m_use,
+                                              ptile + h * kPfHalf, (uint32_t)r, mx)
+                      : pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use,
+                                             ptile + h * kPfHalf, (uint32_t)r, mx);
+          }
+          redo = __any_sync(0xffffffffu, mx * p.scale_log2 > m_ref + kPfRescaleLog2);
+        }
+        if (redo) {
+          // first tile, or the max grew by more than 2^8 somewhere in the warp:
+          // take the exact row max, rescale O where needed, redo the exponentials
+          mx = -INFINITY;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float sv[64];
+            tmem_ld32(lane_addr + col_s + h * 64, sv);
+            tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 64; ++i) mx = fmaxf(mx, h * 64 + i <= lim ? sv[i] : -INFINITY);
+          }
+          const float m_new = fmaxf(m_ref, mx * p.scale_log2);
+          const bool need = m_new > m_ref + kPfRescaleLog2;
+          if (j >= 1 && __any_sync(0xffffffffu, need)) {
+            const float fac = need ? exp2f(m_ref - m_new) : 1.f;
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {
+              float o[16];
+              tmem_ld16(lane_addr + col_o + c * 16, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] *= fac;
+              tmem_st16(lane_addr + col_o + c * 16, o);
+            }
+            tmem_wait_st();
+            l *= fac;
+          }
+          if (j == 0 || need) m_ref = m_new;
+          const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+          rs = 0.f;
+          float mx2 = -INFINITY;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float sv[64];
+            tmem_ld32(lane_addr + col_s + h * 64, sv);
+            tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
+            tmem_wait_ld();
+            rs += pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use, ptile + h * kPfHalf,
+                                       (uint32_t)r, mx2);
+          }
+        }
+        // S_x fully read: release it to the next S MMA
+        tc_fence_before();
+        mbar_arrive(&s_free[x]);
+        l += rs;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&p_full[x]);
       }
-      // pass 2: P = exp2(s*scale - m) -> swizzled K-major tile in shared memory
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(scol + c * 32, v);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float e0 = (c * 32 + i) <= lim ? exp2f(v[i] * p.scale_log2 - m_use) : 0.f;
-          const float e1 = (c * 32 + i + 1) <= lim ? exp2f(v[i + 1] * p.scale_log2 - m_use) : 0.f;
-          rs += e0 + e1;
-          pk[i >> 1] = DT<T>::from_f2(e0, e1);
-        }
-        uint8_t* half = pbase + (c >> 1) * kPfHalf;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t chunk = (uint32_t)((c & 1) * 4 + u);
-          uint4* dst = reinterpret_cast<uint4*>(half + sw128_offset((uint32_t)r, chunk));
-          *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      fence_proxy_async_smem();
-      mbar_arrive(p_full);
-      l = l * alpha + rs;
-      m = m_new;
-      alpha_prev = alpha;
-    }
-    if (alive && ntiles > 0) {
-      if (__all_sync(0xffffffffu, mbar_wait(o_full, (uint32_t)(ntiles - 1) & 1u, p.err))) {
+      if (alive && ntiles > 0 &&
+          __all_sync(0xffffffffu, mbar_wait(&o_done[x], (uint32_t)(ntiles - 1) & 1u, p.err))) {
         tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* dst = reinterpret_cast<T*>(p.out) +
+                 ((int64_t)(qs + qi) * p.num_q_heads + head0 + x) * kPfD;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(lane_addr + kPfColO + c * 32, v);
+          float o[32];
+          tmem_ld32(lane_addr + col_o + c * 32, o);
           tmem_wait_ld();
+          if (qi < q_len) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = acc[c * 32 + i] * alpha_prev + v[i];
+            for (int d = 0; d < 32; d += 8) {
+              uint4 w;
+              w.x = DT<T>::from_f2(o[d] * inv, o[d + 1] * inv);
+              w.y = DT<T>::from_f2(o[d + 2] * inv, o[d + 3] * inv);
+              w.z = DT<T>::from_f2(o[d + 4] * inv, o[d + 5] * inv);
+              w.w = DT<T>::from_f2(o[d + 6] * inv, o[d + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + d) = w;
+            }
+          }
         }
-      }
-    }
-    if (qi < q_len) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* dst = reinterpret_cast<T*>(p.out) + ((int64_t)(qs + qi) * p.num_q_heads + hq) * kPfD;
-#pragma unroll
-      for (int d = 0; d < kPfD; d += 8) {
-        uint4 w;
-        w.x = DT<T>::from_f2(acc[d] * inv, acc[d + 1] * inv);
-        w.y = DT<T>::from_f2(acc[d + 2] * inv, acc[d + 3] * inv);
-        w.z = DT<T>::from_f2(acc[d + 4] * inv, acc[d + 5] * inv);
-        w.w = DT<T>::from_f2(acc[d + 6] * inv, acc[d + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + d) = w;
       }
     }
   }
@@ -417,22 +596,23 @@ int launch_paged_prefill(const AttnArgs& a) {
   p.num_blocks = a.num_blocks;
   p.num_q_heads = a.hq;
   p.group = a.hq / a.hkv;
+  p.pair = (p.group % 2 == 0) ? 1 : 0;  // two heads of one kv group per CTA
   p.page_size = a.page;
   p.num_q_tiles = (a.max_q + kPfBM - 1) / kPfBM;
   p.causal = a.causal;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = device_error_word();
-  dim3 grid(p.num_q_tiles, a.hq, a.num_seqs);
+  dim3 grid(p.num_q_tiles, p.pair ? a.hq / 2 : a.hq, a.num_seqs);
   if (a.dtype == NVKV_DTYPE_BF16) {
     auto kern = paged_prefill_kernel<__nv_bfloat16>;
-    static unsigned long long attr_done_1 = 0;
-    rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done_1);
+    static unsigned long long attr_done_bf16 = 0;
+    rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done_bf16);
     if (rc) return rc;
     kern<<<grid, kPfThreads, kPfSmemBytes, a.stream>>>(mq, mk, mv, p);
   } else {
     auto kern = paged_prefill_kernel<__half>;
-    static unsigned long long attr_done_2 = 0;
-    rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done_2);
+    static unsigned long long attr_done_f16 = 0;
+    rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done_f16);
     if (rc) return rc;
     kern<<<grid, kPfThreads, kPfSmemBytes, a.stream>>>(mq, mk, mv, p);
   }

@@ -51,6 +51,8 @@ SIGNATURES = {
     "nvkv_paged_attention_noalloc": [_p, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64,
                                      _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
                                      _p],
+    "nvkv_rms_norm": [_p, _i64, _p, _i64, _p, _f32, _p, _i64, _i64, _i32, _i32, _p],
+    "nvkv_silu_and_mul": [_p, _i64, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_context_set": [_p, _p, _i32, _i32, _i32, _p, _i64, _p, _p, _i64],
     "nvkv_context_reset": [],
     "nvkv_attention_create": [_f32, ctypes.POINTER(_p)],

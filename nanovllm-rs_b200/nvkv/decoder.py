@@ -2,12 +2,12 @@
 
 This is the caller side of the path (models/qwen3.rs:126-146,179-183,226-297,
 layers/linear.rs, layers/embed_head.rs) restated with torch for everything
-that is NOT one of the path's kernels: the projections are cuBLAS GEMMs, the
-residual RMSNorm / SiLU*mul are torch elementwise ops, and the tensor-parallel
-collectives are NCCL through torch.distributed.  Per layer the attention hot
-path is exactly two nvkv launches: nvkv_qknorm_rope (split_qkv + q/k RMSNorm
-+ RoPE + KV-cache store, fused) and nvkv_paged_attention (split-KV decode or
-tcgen05 prefill).
+that is NOT one of the path's kernels: the projections are cuBLAS GEMMs and
+the tensor-parallel collectives are NCCL through torch.distributed.  Per layer
+the attention hot path is two nvkv launches, nvkv_qknorm_rope (split_qkv +
+q/k RMSNorm + RoPE + KV-cache store, fused) and nvkv_paged_attention
+(split-KV decode or tcgen05 prefill), and the epilogues around it are nvkv's
+fused residual RMSNorm (x2) and SiLU*mul.
 
 Tensor-parallel layout (one process per GPU), as the reference shards it:
   * qkv_proj   column-parallel, local rows [q_r ; k_r ; v_r]  (linear.rs:214-281)
@@ -114,20 +114,6 @@ def gather_logits(local: torch.Tensor, group=None) -> torch.Tensor:
     return torch.cat(parts, dim=-1)
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """layernorm.rs:18-25: f32 statistics, cast, then x weight."""
-    xf = x.float()
-    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return y.to(x.dtype) * w
-
-
-def residual_rms_norm(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float):
-    """layernorm.rs:27-42: returns (normed, new_residual)."""
-    xf = x.float() + res.float()
-    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return y.to(x.dtype) * w, xf.to(x.dtype)
-
-
 # ---------------------------------------------------------------------------
 # Step metadata on the device (what ModelRunner::prepare_model_input uploads)
 # ---------------------------------------------------------------------------
@@ -149,7 +135,8 @@ class Qwen3TP:
     """One rank of a TP-sharded Qwen3 decoder whose attention is the nvkv path."""
 
     def __init__(self, cfg: Qwen3Config, rank: int = 0, tp: int = 1, seed: int = 0,
-                 dtype=torch.bfloat16, device="cuda", init_scale: float = 1.0, group=None):
+                 dtype=torch.bfloat16, device="cuda", init_scale: float = 1.0, group=None,
+                 embed_std: float = 1.0, head_std: Optional[float] = None):
         self.cfg, self.rank, self.tp, self.group = cfg, rank, tp, group
         self.dtype, self.device = dtype, torch.device(device)
         self.hq = divide(cfg.num_attention_heads, tp)
@@ -171,7 +158,7 @@ class Qwen3TP:
             return (1.0 + 0.1 * torch.randn(n, generator=g, device=self.device)).to(dtype)
 
         s_in = init_scale / math.sqrt(H)
-        emb = full(cfg.vocab_size, H, 1.0)
+        emb = full(cfg.vocab_size, H, embed_std)
         self.embed = shard_vocab(emb, rank, tp)
         self.layers = []
         for _ in range(cfg.num_hidden_layers):
@@ -191,7 +178,8 @@ class Qwen3TP:
             L["qn"], L["kn"] = norm_w(D), norm_w(D)
             self.layers.append(L)
         self.norm = norm_w(H)
-        lm = emb if cfg.tie_word_embeddings else full(cfg.vocab_size, H, s_in)
+        lm = emb if cfg.tie_word_embeddings else full(cfg.vocab_size, H,
+                                                       s_in if head_std is None else head_std)
         self.lm_head = shard_vocab(lm, rank, tp)  # tie_weights (qwen3.rs:334-338)
         del emb, lm
         self.k_caches: List[torch.Tensor] = []
@@ -240,35 +228,43 @@ class Qwen3TP:
         ws_n = ops.workspace_size(st.cu_seqlens_q.numel() - 1, self.hq, self.hkv, st.max_seqlen_q,
                                   st.max_seqlen_k, D)
         ws = self._buf("ws", (max(ws_n, 16),), torch.uint8)
+        xb = self._buf("x", (T, cfg.hidden_size))
+        actb = self._buf("act", (T, self.ffn))
+        eps = cfg.rms_norm_eps
         residual = None
         for li, L in enumerate(self.layers):
+            # input_layernorm: forward on the first layer, residual_forward after
+            # (qwen3.rs:232-238); the residual is updated in place to h + residual
             if residual is None:
-                x, residual = rms_norm(h, L["ln1"], cfg.rms_norm_eps), h
+                x, residual = ops.rms_norm(h, L["ln1"], eps, out=xb), h
             else:
-                x, residual = residual_rms_norm(h, residual, L["ln1"], cfg.rms_norm_eps)
+                x = ops.rms_norm(h, L["ln1"], eps, residual=residual, out=xb)
             qkv = torch.matmul(x, L["qkv"].t())
-            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"],
-                            cfg.rms_norm_eps, cfg.rope_theta, cfg.max_position_embeddings, D,
+            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"], eps,
+                            cfg.rope_theta, cfg.max_position_embeddings, D,
                             k_cache=self.k_caches[li], v_cache=self.v_caches[li],
                             slot_mapping=st.slot_mapping, q_out=q_buf)
             ops.paged_attention(q_buf, self.k_caches[li], self.v_caches[li], st.cu_seqlens_q,
                                 st.cu_seqlens_k, st.block_tables, st.max_seqlen_q,
                                 st.max_seqlen_k, self.scale, out=o_buf, workspace=ws)
             a = self._all_reduce(torch.matmul(o_buf.view(T, -1), L["o"].t()))
-            x, residual = residual_rms_norm(a, residual, L["ln2"], cfg.rms_norm_eps)
+            x = ops.rms_norm(a, L["ln2"], eps, residual=residual, out=xb)
             gu = torch.matmul(x, L["gate_up"].t())
-            act = torch.nn.functional.silu(gu[:, :self.ffn]) * gu[:, self.ffn:]
+            act = ops.silu_and_mul(gu, out=actb)
             h = self._all_reduce(torch.matmul(act, L["down"].t()))
-        h, _ = residual_rms_norm(h, residual, self.norm, cfg.rms_norm_eps)
+        h = ops.rms_norm(h, self.norm, eps, residual=residual, out=xb)  # qwen3.rs:295
         last = h.index_select(0, st.last_idx)
-        logits = torch.matmul(last, self.lm_head.t()).float()
+        # bf16 operands, fp32 output: no bf16 rounding of the logits, so the
+        # greedy argmax sees no artificial ties
+        logits = torch.mm(last, self.lm_head.t(), out_dtype=torch.float32)
         return gather_logits(logits, self.group)
 
     def launches_per_step(self, st: Step) -> int:
-        """nvkv kernel launches one forward issues: per layer the prologue,
-        the decode kernel, the combine kernel when the split-KV plan splits,
-        and the prefill kernel when any sequence has q_len > 1."""
+        """nvkv kernel launches one forward issues: per layer two RMSNorms,
+        SiLU*mul, the prologue, the decode kernel, the combine kernel when the
+        split-KV plan splits, and the prefill kernel when any sequence has
+        q_len > 1; plus the final norm."""
         B = st.cu_seqlens_q.numel() - 1
         split = ops.workspace_size(B, self.hq, self.hkv, st.max_seqlen_q, st.max_seqlen_k) > 0
-        per = 2 + (1 if split else 0) + (1 if st.max_seqlen_q > 1 else 0)
-        return per * self.cfg.num_hidden_layers
+        per = 5 + (1 if split else 0) + (1 if st.max_seqlen_q > 1 else 0)
+        return per * self.cfg.num_hidden_layers + 1

@@ -157,3 +157,35 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         int(max_seqlen_q), int(max_seqlen_k), hq, hkv, d, page, float(softmax_scale),
         1 if causal else 0, _ptr(workspace), ws_bytes, _dtype(q), _stream()))
     return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+             residual: Optional[torch.Tensor] = None,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RMSNorm::forward / residual_forward (layernorm.rs:18-42) in one launch.
+    With `residual`, it is updated in place to dtype(x + residual) and the
+    norm is taken of that sum (the reference returns it as the new residual)."""
+    _need(x.is_cuda and x.dim() == 2 and x.stride(1) == 1, "x must be [T, H] on cuda")
+    T, H = x.shape
+    _need(weight.dtype == x.dtype and weight.is_contiguous() and weight.numel() == H, "weight")
+    if residual is not None:
+        _need(residual.shape == x.shape and residual.stride(1) == 1 and
+              residual.dtype == x.dtype, "residual must match x")
+    if out is None:
+        out = torch.empty_like(x)
+    check(lib.nvkv_rms_norm(_ptr(x), x.stride(0), _ptr(residual),
+                            0 if residual is None else residual.stride(0), _ptr(weight),
+                            float(eps), _ptr(out), out.stride(0), T, H, _dtype(x), _stream()))
+    return out
+
+
+def silu_and_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """SiluAndMul::forward (activation.rs:5-17): silu(gate) * up in one launch."""
+    _need(gate_up.is_cuda and gate_up.dim() == 2 and gate_up.stride(1) == 1, "gate_up: [T, 2F]")
+    T, W = gate_up.shape
+    F = W // 2
+    if out is None:
+        out = torch.empty(T, F, device=gate_up.device, dtype=gate_up.dtype)
+    check(lib.nvkv_silu_and_mul(_ptr(gate_up), gate_up.stride(0), _ptr(out), out.stride(0), T, F,
+                                _dtype(gate_up), _stream()))
+    return out

@@ -309,6 +309,25 @@ def rms_norm(x, weight, eps: float, dtype: str) -> np.ndarray:
     return round_to(normed * np.asarray(weight, np.float32), dtype)
 
 
+def residual_rms_norm(x, residual, weight, eps: float, dtype: str):
+    """layers/layernorm.rs:27-42: s = x + residual in f32; returns
+    (dtype(dtype(s * rsqrt(mean(s^2) + eps)) * w), dtype(s))."""
+    s = np.asarray(x, np.float32) + np.asarray(residual, np.float32)
+    var = np.mean(s * s, axis=-1, keepdims=True, dtype=np.float32)
+    inv = np.float32(1.0) / np.sqrt(var + np.float32(eps))
+    out = round_to(round_to(s * inv, dtype) * np.asarray(weight, np.float32), dtype)
+    return out, round_to(s, dtype)
+
+
+def silu_and_mul(gate_up, dtype: str):
+    """layers/activation.rs:5-17: dtype(dtype(silu(g)) * u), silu in f32."""
+    gu = np.asarray(gate_up, np.float32)
+    F = gu.shape[-1] // 2
+    g, u = gu[..., :F], gu[..., F:]
+    silu = round_to(g / (np.float32(1.0) + np.exp(-g)), dtype)
+    return round_to(silu * u, dtype)
+
+
 def rope_inv_freq(head_dim: int, base: float) -> np.ndarray:
     """layers/rotary_embedding.rs:31-37: 1/exp((2i/D)*ln(base)) in f32."""
     exponent = np.arange(0, head_dim, 2, dtype=np.float32) / np.float32(head_dim)
