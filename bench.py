@@ -158,7 +158,7 @@ def _dist_setup():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     return rank, world, dev
 
 
@@ -228,10 +228,10 @@ def run_nvkv(a):
     sampler = ClockSampler(bus) if rank == 0 else None
 
     # ---- timed region: K decode steps, inputs resident in HBM ----
-    _barrier(world)
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        time.sleep(0.3)  # before the barrier: every rank enters the timed region together
+    _barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("bench_timed")  # ncu --nvtx-include "bench_timed/"
     e0.record()
@@ -313,10 +313,15 @@ def run_nvkv(a):
         if world == 1:
             line["cpu_baseline"] = cpu_reference(max_seconds=20.0)
         print(json.dumps(line), flush=True)
+    # a graph holding NCCL calls must be released before the process group
+    run = None
     if graph is not None:
-        del graph
+        graph.reset()
+        graph = None
+    torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -374,11 +379,25 @@ def _cpu_one(model, ids, pos, ctx):
     return time.perf_counter() - t0
 
 
+def _all_host_threads():
+    """torchrun sets OMP_NUM_THREADS=1; the CPU arm uses every host core."""
+    import threadpoolctl
+    n = os.cpu_count() or 1
+    threadpoolctl.threadpool_limits(limits=n)
+    try:
+        import torch
+        torch.set_num_threads(n)
+    except Exception:
+        pass
+    return n
+
+
 def cpu_reference(max_seconds=20.0, reps=None, warmup=1, num_tokens=32, layers=2, vocab_frac=32):
     """Times the CPU restatement on a bounded sample of the same decode step:
     `num_tokens` of the 256 sequences through `layers` of the 36 layers and a
     1/`vocab_frac` slice of lm_head; the step time is scaled by
     (256/num_tokens) * (36/layers) for the layers and likewise for the head."""
+    _all_host_threads()
     model, ids, pos, ctx, cfg = _cpu_sample_setup(num_tokens, layers, vocab_frac)
     for _ in range(warmup):
         _cpu_one(model, ids, pos, ctx)
@@ -416,6 +435,7 @@ def run_reference(a):
     world = int(os.environ.get("WORLD_SIZE", 1))
     if rank != 0:
         return
+    _all_host_threads()
     model, ids, pos, ctx, cfg = _cpu_sample_setup()
     for _ in range(max(a.warmup, 1)):
         _cpu_one(model, ids, pos, ctx)

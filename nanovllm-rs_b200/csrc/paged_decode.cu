@@ -347,13 +347,19 @@ __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParam
 
 // Split-KV plan: enough CTAs for ~3 resident waves at 2 CTAs/SM, but never
 // chunks shorter than 4 tiles (256 keys) so per-CTA setup stays amortised.
+#ifndef NVKV_DECODE_TARGET_CTAS
+#define NVKV_DECODE_TARGET_CTAS (148 * 2 * 3)
+#endif
+#ifndef NVKV_DECODE_MIN_TILES
+#define NVKV_DECODE_MIN_TILES 4
+#endif
 void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
                  int* max_splits) {
   const int tiles = max_seqlen_k > 0 ? (max_seqlen_k + kDecTile - 1) / kDecTile : 1;
   const int64_t items = (int64_t)num_seqs * num_kv_heads;
-  const int64_t target = 148 * 2 * 3;
+  const int64_t target = NVKV_DECODE_TARGET_CTAS;
   int splits = (int)((target + items - 1) / items);
-  const int max_by_len = (tiles + 3) / 4;
+  const int max_by_len = (tiles + NVKV_DECODE_MIN_TILES - 1) / NVKV_DECODE_MIN_TILES;
   if (splits > max_by_len) splits = max_by_len;
   if (splits < 1) splits = 1;
   const int tiles_per_split = (tiles + splits - 1) / splits;
