@@ -320,7 +320,15 @@ def run_nvkv(a):
         graph = None
     torch.cuda.synchronize()
     if world > 1:
+        import threading
         import torch.distributed as dist
+
+        # every GPU result is final here; never let communicator teardown hold the job
+        def _exit_if_stuck():
+            time.sleep(30)
+            os._exit(0)
+
+        threading.Thread(target=_exit_if_stuck, daemon=True).start()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -99,6 +99,9 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     }
     fence_mbar_init();
   }
+  // let the (tiny) split-KV combine grid be scheduled while this grid's last
+  // wave runs; it waits on griddepcontrol.wait for this grid's results
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
 
   if (warp == kDecComputeWarps) {
@@ -318,8 +321,12 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 
 // Merge of the split-KV partials of one (sequence, query head): weights
 // 2^(lse_s - max lse), the standard log-sum-exp combine.
+// Launched as a programmatic dependent of the decode kernel: its CTAs may be
+// scheduled while the decode grid drains, and griddepcontrol.wait holds them
+// until that grid has completed and its partials are visible.
 template <typename T>
 __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int hq = blockIdx.x, b = blockIdx.y;
   const uint32_t q0 = p.cu_q[b];
   if (p.cu_q[b + 1] - q0 != 1) return;
@@ -346,12 +353,14 @@ __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParam
 // ---------------------------------------------------------------------------
 
 // Split-KV plan: enough CTAs for ~3 resident waves at 2 CTAs/SM, but never
-// chunks shorter than 4 tiles (256 keys) so per-CTA setup stays amortised.
+// chunks shorter than 12 tiles (768 keys): a sweep over the decode shapes of
+// configs 2, 4 (TP1, TP8) and 5 found this the best or equal-best everywhere
+// (shorter chunks pay per-CTA setup and merge work on small per-GPU batches).
 #ifndef NVKV_DECODE_TARGET_CTAS
 #define NVKV_DECODE_TARGET_CTAS (148 * 2 * 3)
 #endif
 #ifndef NVKV_DECODE_MIN_TILES
-#define NVKV_DECODE_MIN_TILES 4
+#define NVKV_DECODE_MIN_TILES 12
 #endif
 void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
                  int* max_splits) {
@@ -373,6 +382,22 @@ size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, i
   if (splits <= 1) return 0;
   const size_t n = (size_t)num_seqs * splits * num_q_heads;
   return n * kDecD * sizeof(float) + n * sizeof(float) + 256;
+}
+
+// The combine launch overlaps the decode grid's tail (programmatic stream
+// serialisation); the kernel's griddepcontrol.wait keeps the data order.
+static int launch_combine(void (*kern)(DecodeParams), const DecodeParams& p, const AttnArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.hq, a.num_seqs);
+  cfg.blockDim = dim3(kDecD);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "decode combine launch");
 }
 
 int launch_paged_decode(const AttnArgs& a) {
@@ -416,16 +441,20 @@ int launch_paged_decode(const AttnArgs& a) {
     rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_1);
     if (rc) return rc;
     kern<<<grid, kDecThreads, kDecSmemBytes, a.stream>>>(mk, mv, p);
-    if (splits > 1)
-      decode_combine_kernel<__nv_bfloat16><<<dim3(a.hq, a.num_seqs), kDecD, 0, a.stream>>>(p);
+    if (splits > 1) {
+      rc = launch_combine(decode_combine_kernel<__nv_bfloat16>, p, a);
+      if (rc) return rc;
+    }
   } else {
     auto kern = paged_decode_kernel<__half>;
     static unsigned long long attr_done_2 = 0;
     rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_2);
     if (rc) return rc;
     kern<<<grid, kDecThreads, kDecSmemBytes, a.stream>>>(mk, mv, p);
-    if (splits > 1)
-      decode_combine_kernel<__half><<<dim3(a.hq, a.num_seqs), kDecD, 0, a.stream>>>(p);
+    if (splits > 1) {
+      rc = launch_combine(decode_combine_kernel<__half>, p, a);
+      if (rc) return rc;
+    }
   }
   return check_cuda(cudaGetLastError(), "paged decode launch");
 }

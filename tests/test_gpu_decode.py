@@ -75,7 +75,7 @@ def test_decode_gqa_groups(group):
 
 
 def test_decode_long_context_many_splits():
-    """Few (sequence, kv-head) items -> many splits + the LSE combine kernel
+    """Few (sequence, kv-head) items -> many splits + the in-kernel LSE merge
     (the 32B-at-TP8 shape: 1 kv head per GPU, 8 q heads)."""
     _decode_case([32768, 5000, 257], 8, 1, seed=9)
 
@@ -110,3 +110,59 @@ def test_decode_block_id_out_of_range_is_reported():
     torch.cuda.synchronize()
     assert nvkv.device_error() == nvkv._lib.DEVERR_BLOCK_RANGE
     assert torch.isfinite(out.float()).all()
+
+
+def _split_case(lens, hq, hkv, seed):
+    g = torch.Generator().manual_seed(seed)
+    nb = sum((L + 255) // 256 for L in lens) + 2
+    kc, vc, bt, tables = make_paged(lens, 256, hkv, 128, nb, g)
+    q = torch.randn(len(lens), hq, 128, generator=g).to(torch.bfloat16).cuda()
+    return q, kc, vc, torch.from_numpy(bt.view(np.int32)).cuda(), tables
+
+
+def _oracle(q, kc, vc, tables, lens):
+    qn = f32(q)
+    return np.concatenate([O.causal_attention_one(qn[b:b + 1], *gather_seq(kc, vc, tables[b], L),
+                                                  128 ** -0.5) for b, L in enumerate(lens)])
+
+
+def test_decode_workspace_reused_across_shapes_with_garbage():
+    """The split-KV merge counters live in the caller's workspace: stale bytes
+    from other calls (or garbage) must not matter."""
+    ws = torch.randint(0, 256, (64 << 20,), dtype=torch.uint8, device="cuda")
+    cases = [([5000, 3000, 8000], 8, 1, 1), ([2000] * 40, 16, 8, 2), ([5000, 3000, 8000], 8, 1, 1),
+             ([700, 32768], 16, 2, 3)]
+    for lens, hq, hkv, seed in cases:
+        q, kc, vc, bt, tables = _split_case(lens, hq, hkv, seed)
+        assert nvkv.workspace_size(len(lens), hq, hkv, 1, max(lens)) > 0
+        out = nvkv.paged_attention(q, kc, vc, cu([1] * len(lens)), cu(lens), bt, 1, max(lens),
+                                   128 ** -0.5, workspace=ws)
+        torch.cuda.synchronize()
+        assert_attention_close(out, _oracle(q, kc, vc, tables, lens), f"{lens}")
+    assert nvkv.device_error() == 0
+
+
+def test_decode_graph_replays_reuse_the_merge_counters():
+    lens, hq, hkv = [9000, 2500, 4100, 600], 8, 2
+    q, kc, vc, bt, tables = _split_case(lens, hq, hkv, 4)
+    ws = torch.zeros(nvkv.workspace_size(len(lens), hq, hkv, 1, max(lens)), dtype=torch.uint8,
+                     device="cuda")
+    out = torch.empty_like(q)
+    cq, ck = cu([1] * len(lens)), cu(lens)
+    run = lambda: nvkv.paged_attention(q, kc, vc, cq, ck, bt, 1, max(lens), 128 ** -0.5,  # noqa
+                                       out=out, workspace=ws)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        run()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    g = torch.Generator().manual_seed(9)
+    for _ in range(3):
+        q.copy_(torch.randn(q.shape, generator=g).to(torch.bfloat16))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert_attention_close(out, _oracle(q, kc, vc, tables, lens), "replay")
+    graph.reset()
