@@ -15,6 +15,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/nvkv.h"
 
@@ -72,19 +73,56 @@ struct AttnArgs {
 };
 
 int launch_paged_decode(const AttnArgs& a);
-int launch_paged_prefill(const AttnArgs& a);
+size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k);
 void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
                  int* max_splits);
-size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k);
+int launch_paged_prefill(const AttnArgs& a);
 int launch_store_kvcache(const void* key, const void* value, void* k_cache, void* v_cache,
                          const int64_t* slot_mapping, int64_t num_tokens, int64_t row_elems,
                          int64_t key_stride, int64_t value_stride, int64_t num_slots,
                          cudaStream_t stream);
 
+// Launch as a programmatic dependent of the previous kernel in the stream
+// (PDL): the grid may be scheduled while that kernel drains, and the kernel
+// must execute griddepcontrol.wait (pdl_wait below) before it reads any
+// input.  After a non-kernel stream operation the attribute has no effect.
+// NVKV_NO_PDL turns the attribute off (A/B builds).
+#ifdef __CUDACC__
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+#ifdef NVKV_NO_PDL
+  cfg.numAttrs = 0;
+#else
+  cfg.numAttrs = 1;
+#endif
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+}
+#endif
+
 // ---------------------------------------------------------------------------
 // Device helpers
 // ---------------------------------------------------------------------------
 #ifdef __CUDACC__
+
+// Waits until the grid this one programmatically depends on has completed and
+// its memory is visible (no-op for a normally launched grid).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the dependent grid of this one be scheduled (it still waits for this
+// grid's completion in its own pdl_wait).
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);

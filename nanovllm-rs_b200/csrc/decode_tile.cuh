@@ -1,0 +1,180 @@
+// Per-tile arithmetic of the paged decode kernel: one compute warp, 16 keys
+// of a 64-key K/V tile staged in shared memory by TMA (SWIZZLE_128B), all
+// g = Hq/Hkv query heads of the kv group as the M = 16 rows of m16n8k16 MMAs.
+#pragma once
+
+#include "common.cuh"
+
+namespace nvkv {
+
+constexpr int kDecD = 128;
+constexpr int kDecTile = 64;
+constexpr int kDecStages = 3;
+constexpr int kDecComputeWarps = 4;
+constexpr int kDecThreads = (kDecComputeWarps + 1) * 32;
+constexpr int kDecHalfBytes = kDecTile * 128;      // 64 rows x 64 elems x 2 B
+constexpr int kDecTileBytes = 2 * kDecHalfBytes;   // one K (or V) tile
+constexpr int kDecStageBytes = 2 * kDecTileBytes;  // K + V
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_u32(const void* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+// A fragments of the g query rows (rows >= g are zero), D = 128 as 8 k-steps.
+template <typename T>
+__device__ __forceinline__ void dec_load_q(uint32_t (&qa)[8][4], const T* qrow, int g, int lane) {
+  const int r0 = lane >> 2, r1 = r0 + 8;
+  const int cq = (lane & 3) * 2;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int d = kk * 16 + cq;
+    qa[kk][0] = r0 < g ? ld_u32(qrow + r0 * kDecD + d) : 0u;
+    qa[kk][1] = r1 < g ? ld_u32(qrow + r1 * kDecD + d) : 0u;
+    qa[kk][2] = r0 < g ? ld_u32(qrow + r0 * kDecD + d + 8) : 0u;
+    qa[kk][3] = r1 < g ? ld_u32(qrow + r1 * kDecD + d + 8) : 0u;
+  }
+}
+
+// Online-softmax state of one warp: O rows r0 = lane/4 and r1 = r0 + 8.
+struct DecState {
+  float o[16][4];
+  float m0, m1, l0, l1;
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  }
+};
+
+// This warp's 16 keys [wtok, wtok + 16) of the tile at kbase / vbase (shared
+// addresses); `valid` = how many of them exist (<= 0: nothing to do).
+// S = Q.K^T (two n8 key tiles), fp32 online softmax with quad shuffles, then
+// O += P.V with P re-packed from the S accumulators as the A operand and
+// the V fragments of missing keys zeroed (stale cache rows never reach O).
+template <typename T>
+__device__ __forceinline__ void dec_tile(const uint32_t (&qa)[8][4], DecState& st, uint32_t kbase,
+                                         uint32_t vbase, int wtok, int valid, float scale_log2,
+                                         int lane) {
+  const int cq = (lane & 3) * 2;
+  const int lrow = lane & 7;   // row inside an 8x8 ldmatrix tile
+  const int lmat = lane >> 3;  // which of the four 8x8 tiles this lane addresses
+  float sc[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    const uint32_t krow = (uint32_t)(wtok + nt * 8 + lrow);
+#pragma unroll
+    for (int kk = 0; kk < 8; kk += 2) {
+      const uint32_t chunk = (uint32_t)(2 * kk + lmat);  // 16-byte chunk along D (0..15)
+      const uint32_t addr = kbase + (chunk >> 3) * kDecHalfBytes + sw128_offset(krow, chunk & 7);
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(b0, b1, b2, b3, addr);
+      mma_16816<T>(sc[nt], qa[kk], b0, b1);
+      mma_16816<T>(sc[nt], qa[kk + 1], b2, b3);
+    }
+  }
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const bool ok = (nt * 8 + cq + e) < valid;
+      sc[nt][e] = ok ? sc[nt][e] * scale_log2 : -INFINITY;
+      sc[nt][e + 2] = ok ? sc[nt][e + 2] * scale_log2 : -INFINITY;
+      mx0 = fmaxf(mx0, sc[nt][e]);
+      mx1 = fmaxf(mx1, sc[nt][e + 2]);
+    }
+  }
+  mx0 = warp_max_xor(warp_max_xor(mx0, 1), 2);
+  mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
+  const float mn0 = fmaxf(st.m0, mx0), mn1 = fmaxf(st.m1, mx1);
+  const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+  const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+  const float al0 = exp2f(st.m0 - mu0), al1 = exp2f(st.m1 - mu1);
+  st.m0 = mn0;
+  st.m1 = mn1;
+  float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sc[nt][e] = exp2f(sc[nt][e] - mu0);
+      sc[nt][e + 2] = exp2f(sc[nt][e + 2] - mu1);
+      ps0 += sc[nt][e];
+      ps1 += sc[nt][e + 2];
+    }
+  }
+  st.l0 = st.l0 * al0 + ps0;
+  st.l1 = st.l1 * al1 + ps1;
+  if (al0 != 1.f || al1 != 1.f) {
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      st.o[n][0] *= al0;
+      st.o[n][1] *= al0;
+      st.o[n][2] *= al1;
+      st.o[n][3] *= al1;
+    }
+  }
+  uint32_t pa[4];
+  pa[0] = DT<T>::from_f2(sc[0][0], sc[0][1]);
+  pa[1] = DT<T>::from_f2(sc[0][2], sc[0][3]);
+  pa[2] = DT<T>::from_f2(sc[1][0], sc[1][1]);
+  pa[3] = DT<T>::from_f2(sc[1][2], sc[1][3]);
+  // keys this lane's B fragments carry: wtok + cq + {0,1} (b0), + 8 (b1)
+  const uint32_t keep_lo = (cq < valid ? 0x0000ffffu : 0u) | (cq + 1 < valid ? 0xffff0000u : 0u);
+  const uint32_t keep_hi =
+      (cq + 8 < valid ? 0x0000ffffu : 0u) | (cq + 9 < valid ? 0xffff0000u : 0u);
+  const uint32_t vrow = (uint32_t)(wtok + (lmat & 1) * 8 + lrow);
+#pragma unroll
+  for (int dn = 0; dn < 16; dn += 2) {
+    const uint32_t chunk = (uint32_t)(dn + (lmat >> 1));
+    const uint32_t addr = vbase + (chunk >> 3) * kDecHalfBytes + sw128_offset(vrow, chunk & 7);
+    uint32_t b0, b1, b2, b3;
+    ldmatrix_x4_trans(b0, b1, b2, b3, addr);
+    b0 &= keep_lo;
+    b1 &= keep_hi;
+    b2 &= keep_lo;
+    b3 &= keep_hi;
+    mma_16816<T>(st.o[dn], pa, b0, b1);
+    mma_16816<T>(st.o[dn + 1], pa, b2, b3);
+  }
+}
+
+// TMA row of key tile j0 of sequence b: through the page table (pages of
+// page_size rows; an out-of-range page id is recorded and read as page 0 so
+// the waiting consumers still get their bytes) or contiguous from cu_k[b].
+__device__ __forceinline__ int64_t dec_tile_row(const uint32_t* block_tables, int64_t bt_stride,
+                                                int64_t num_blocks, int page_size,
+                                                const uint32_t* cu_k, int b, int j0, int* err) {
+  if (block_tables) {
+    uint32_t page = block_tables[(int64_t)b * bt_stride + j0 / page_size];
+    if ((int64_t)page >= num_blocks) {
+      record_error(err, NVKV_DEVERR_BLOCK_RANGE);
+      page = 0;
+    }
+    return (int64_t)page * page_size + (j0 % page_size);
+  }
+  return (int64_t)cu_k[b] + j0;
+}
+
+// Four TMA loads of one stage: K and V, the two 64-element halves of D.
+__device__ __forceinline__ void dec_load_stage(uint8_t* st, uint64_t* full, const CUtensorMap* mk,
+                                               const CUtensorMap* mv, int kvh, int64_t row) {
+  mbar_arrive_expect_tx(full, kDecStageBytes);
+  tma_load_3d(st, mk, full, 0, kvh, (int)row);
+  tma_load_3d(st + kDecHalfBytes, mk, full, 64, kvh, (int)row);
+  tma_load_3d(st + kDecTileBytes, mv, full, 0, kvh, (int)row);
+  tma_load_3d(st + kDecTileBytes + kDecHalfBytes, mv, full, 64, kvh, (int)row);
+}
+
+}  // namespace nvkv

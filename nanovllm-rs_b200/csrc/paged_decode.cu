@@ -20,21 +20,12 @@
 //
 // Roofline: HBM.  Algorithmic bytes per (sequence, kv head) = 2*L*D*2 (K, V)
 // plus q/out rows; nothing is re-read across query heads.
-#include "common.cuh"
+#include "decode_tile.cuh"
 
 namespace nvkv {
 
-constexpr int kDecD = 128;
-constexpr int kDecTile = 64;
-constexpr int kDecStages = 3;
-constexpr int kDecComputeWarps = 4;
-constexpr int kDecThreads = (kDecComputeWarps + 1) * 32;
-constexpr int kDecHalfBytes = kDecTile * 128;          // 64 rows x 64 elems x 2 B
-constexpr int kDecTileBytes = 2 * kDecHalfBytes;       // one K (or V) tile
-constexpr int kDecStageBytes = 2 * kDecTileBytes;      // K + V
 constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + 2 * kDecStages * 8 +
                               kDecComputeWarps * 2 * 16 * 4 + 1024;
-constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
   const void* q;
@@ -56,18 +47,6 @@ struct DecodeParams {
   int* err;
 };
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
-
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_u32(const void* p) {
-  return *reinterpret_cast<const uint32_t*>(p);
-}
-
 template <typename T>
 __global__ void __launch_bounds__(kDecThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
@@ -78,8 +57,29 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   uint64_t* empty = full + kDecStages;
   float* red = reinterpret_cast<float*>(empty + kDecStages);  // [warp][m|l][16]
 
+#ifdef NVKV_DECODE_SPLIT_MAJOR
+  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+#else
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kDecComputeWarps);
+    }
+    fence_mbar_init();
+  }
+  if (threadIdx.x == kDecComputeWarps * 32) {
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  // let the (tiny) split-KV combine grid be scheduled while this grid's last
+  // wave runs; it waits on griddepcontrol.wait for this grid's results
+  pdl_launch_dependents();
+  pdl_wait();  // inputs may come from the previous kernel in the stream
 
   const uint32_t q0 = p.cu_q[b];
   if (p.cu_q[b + 1] - q0 != 1) return;  // not a decode row: the prefill kernel owns it
@@ -90,47 +90,18 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   const int tok_end = min(k_len, tok_begin + p.chunk_tokens);
   const int ntiles = tok_end > tok_begin ? (tok_end - tok_begin + kDecTile - 1) / kDecTile : 0;
   if (k_len <= 0 && threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
-
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int s = 0; s < kDecStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kDecComputeWarps);
-    }
-    fence_mbar_init();
-  }
-  // let the (tiny) split-KV combine grid be scheduled while this grid's last
-  // wave runs; it waits on griddepcontrol.wait for this grid's results
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
 
   if (warp == kDecComputeWarps) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
       for (int it = 0; it < ntiles; ++it) {
         const int s = it % kDecStages;
         const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
         if (it >= kDecStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
-        const int j0 = tok_begin + it * kDecTile;
-        int64_t row;
-        if (p.block_tables) {
-          uint32_t page = p.block_tables[(int64_t)b * p.bt_stride + j0 / p.page_size];
-          if ((int64_t)page >= p.num_blocks) {
-            record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
-            page = 0;
-          }
-          row = (int64_t)page * p.page_size + (j0 % p.page_size);
-        } else {
-          row = (int64_t)p.cu_k[b] + j0;
-        }
-        uint8_t* st = smem + s * kDecStageBytes;
-        mbar_arrive_expect_tx(&full[s], kDecStageBytes);
-        tma_load_3d(st, &tmap_k, &full[s], 0, kvh, (int)row);
-        tma_load_3d(st + kDecHalfBytes, &tmap_k, &full[s], 64, kvh, (int)row);
-        tma_load_3d(st + kDecTileBytes, &tmap_v, &full[s], 0, kvh, (int)row);
-        tma_load_3d(st + kDecTileBytes + kDecHalfBytes, &tmap_v, &full[s], 64, kvh, (int)row);
+        const int64_t row = dec_tile_row(p.block_tables, p.bt_stride, p.num_blocks, p.page_size,
+                                         p.cu_k, b, tok_begin + it * kDecTile, p.err);
+        dec_load_stage(smem + s * kDecStageBytes, &full[s], &tmap_k, &tmap_v, kvh, row);
       }
     }
     return;
@@ -141,135 +112,34 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   const int hq0 = kvh * g;
   const int r0 = lane >> 2, r1 = r0 + 8;
   const int cq = (lane & 3) * 2;
-  const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)q0 * p.q_stride + (int64_t)hq0 * kDecD;
-
   uint32_t qa[8][4];
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const int d = kk * 16 + cq;
-    qa[kk][0] = r0 < g ? ld_u32(qrow + r0 * kDecD + d) : 0u;
-    qa[kk][1] = r1 < g ? ld_u32(qrow + r1 * kDecD + d) : 0u;
-    qa[kk][2] = r0 < g ? ld_u32(qrow + r0 * kDecD + d + 8) : 0u;
-    qa[kk][3] = r1 < g ? ld_u32(qrow + r1 * kDecD + d + 8) : 0u;
-  }
-
-  float o[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-  const int lrow = lane & 7;   // row inside an 8x8 ldmatrix tile
-  const int lmat = lane >> 3;  // which of the four 8x8 tiles this lane addresses
+  dec_load_q<T>(qa, reinterpret_cast<const T*>(p.q) + (int64_t)q0 * p.q_stride + (int64_t)hq0 * kDecD,
+                g, lane);
+  DecState st;
+  st.reset();
 
   for (int it = 0; it < ntiles; ++it) {
     const int s = it % kDecStages;
     const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
     if (!mbar_wait(&full[s], ph, p.err)) break;
     const uint32_t kbase = smem_u32(smem + s * kDecStageBytes);
-    const uint32_t vbase = kbase + kDecTileBytes;
-    const int tile0 = tok_begin + it * kDecTile;  // first key of the tile
-    const int wtok = warp * 16;                   // this warp's 16 keys inside the tile
-    const int valid = tok_end - (tile0 + wtok);   // keys of this slice that exist
-
-    if (valid > 0) {
-      // ---- S = Q K^T  (two n8 tiles of keys) ----
-      float sc[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-        const uint32_t krow = (uint32_t)(wtok + nt * 8 + lrow);
-#pragma unroll
-        for (int kk = 0; kk < 8; kk += 2) {
-          const uint32_t chunk = (uint32_t)(2 * kk + lmat);  // 16-byte chunk along D (0..15)
-          const uint32_t addr = kbase + (chunk >> 3) * kDecHalfBytes + sw128_offset(krow, chunk & 7);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(b0, b1, b2, b3, addr);
-          mma_16816<T>(sc[nt], qa[kk], b0, b1);
-          mma_16816<T>(sc[nt], qa[kk + 1], b2, b3);
-        }
-      }
-      // ---- masking + online softmax (rows r0 / r1, quad-reduced) ----
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const bool ok = (nt * 8 + cq + e) < valid;
-          sc[nt][e] = ok ? sc[nt][e] * p.scale_log2 : -INFINITY;
-          sc[nt][e + 2] = ok ? sc[nt][e + 2] * p.scale_log2 : -INFINITY;
-          mx0 = fmaxf(mx0, sc[nt][e]);
-          mx1 = fmaxf(mx1, sc[nt][e + 2]);
-        }
-      }
-      mx0 = warp_max_xor(warp_max_xor(mx0, 1), 2);
-      mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
-      const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-      const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-      m0 = mn0;
-      m1 = mn1;
-      float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          sc[nt][e] = exp2f(sc[nt][e] - mu0);
-          sc[nt][e + 2] = exp2f(sc[nt][e + 2] - mu1);
-          ps0 += sc[nt][e];
-          ps1 += sc[nt][e + 2];
-        }
-      }
-      l0 = l0 * al0 + ps0;
-      l1 = l1 * al1 + ps1;
-      if (al0 != 1.f || al1 != 1.f) {
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          o[n][0] *= al0;
-          o[n][1] *= al0;
-          o[n][2] *= al1;
-          o[n][3] *= al1;
-        }
-      }
-      uint32_t pa[4];
-      pa[0] = DT<T>::from_f2(sc[0][0], sc[0][1]);
-      pa[1] = DT<T>::from_f2(sc[0][2], sc[0][3]);
-      pa[2] = DT<T>::from_f2(sc[1][0], sc[1][1]);
-      pa[3] = DT<T>::from_f2(sc[1][2], sc[1][3]);
-
-      // ---- O += P V  (16 n8 tiles along D) ----
-      // keys this lane's B fragments carry: wtok + cq + {0,1} (b0), + 8 (b1)
-      const uint32_t keep_lo = (cq < valid ? 0x0000ffffu : 0u) | (cq + 1 < valid ? 0xffff0000u : 0u);
-      const uint32_t keep_hi =
-          (cq + 8 < valid ? 0x0000ffffu : 0u) | (cq + 9 < valid ? 0xffff0000u : 0u);
-      const uint32_t vrow = (uint32_t)(wtok + (lmat & 1) * 8 + lrow);
-#pragma unroll
-      for (int dn = 0; dn < 16; dn += 2) {
-        const uint32_t chunk = (uint32_t)(dn + (lmat >> 1));
-        const uint32_t addr = vbase + (chunk >> 3) * kDecHalfBytes + sw128_offset(vrow, chunk & 7);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(b0, b1, b2, b3, addr);
-        b0 &= keep_lo;
-        b1 &= keep_hi;
-        b2 &= keep_lo;
-        b3 &= keep_hi;
-        mma_16816<T>(o[dn], pa, b0, b1);
-        mma_16816<T>(o[dn + 1], pa, b2, b3);
-      }
-    }
+    const int valid = tok_end - (tok_begin + it * kDecTile + warp * 16);  // keys of this slice
+    if (valid > 0)
+      dec_tile<T>(qa, st, kbase, kbase + kDecTileBytes, warp * 16, valid, p.scale_log2, lane);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
 
   // ------------------------------ warp combine ------------------------------
+  float l0 = st.l0, l1 = st.l1;
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   if ((lane & 3) == 0) {
-    red[(warp * 2 + 0) * 16 + r0] = m0;
+    red[(warp * 2 + 0) * 16 + r0] = st.m0;
     red[(warp * 2 + 1) * 16 + r0] = l0;
-    red[(warp * 2 + 0) * 16 + r1] = m1;
+    red[(warp * 2 + 0) * 16 + r1] = st.m1;
     red[(warp * 2 + 1) * 16 + r1] = l1;
   }
   named_bar_sync(1, kDecComputeWarps * 32);  // all loops done: stage memory is free
@@ -282,14 +152,14 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       ms0 = fmaxf(ms0, red[(w * 2) * 16 + r0]);
       ms1 = fmaxf(ms1, red[(w * 2) * 16 + r1]);
     }
-    const float f0 = exp2f(m0 - (ms0 == -INFINITY ? 0.f : ms0));
-    const float f1 = exp2f(m1 - (ms1 == -INFINITY ? 0.f : ms1));
+    const float f0 = exp2f(st.m0 - (ms0 == -INFINITY ? 0.f : ms0));
+    const float f1 = exp2f(st.m1 - (ms1 == -INFINITY ? 0.f : ms1));
     float* ow = ofin + warp * 16 * kDecD;
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       const int d = n * 8 + cq;
-      *reinterpret_cast<float2*>(ow + r0 * kDecD + d) = make_float2(o[n][0] * f0, o[n][1] * f0);
-      *reinterpret_cast<float2*>(ow + r1 * kDecD + d) = make_float2(o[n][2] * f1, o[n][3] * f1);
+      *reinterpret_cast<float2*>(ow + r0 * kDecD + d) = make_float2(st.o[n][0] * f0, st.o[n][1] * f0);
+      *reinterpret_cast<float2*>(ow + r1 * kDecD + d) = make_float2(st.o[n][2] * f1, st.o[n][3] * f1);
     }
   }
   named_bar_sync(1, kDecComputeWarps * 32);
@@ -326,7 +196,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 // until that grid has completed and its partials are visible.
 template <typename T>
 __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParams p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_wait();
   const int hq = blockIdx.x, b = blockIdx.y;
   const uint32_t q0 = p.cu_q[b];
   if (p.cu_q[b + 1] - q0 != 1) return;
@@ -387,17 +257,8 @@ size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, i
 // The combine launch overlaps the decode grid's tail (programmatic stream
 // serialisation); the kernel's griddepcontrol.wait keeps the data order.
 static int launch_combine(void (*kern)(DecodeParams), const DecodeParams& p, const AttnArgs& a) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.hq, a.num_seqs);
-  cfg.blockDim = dim3(kDecD);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = a.stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "decode combine launch");
+  return launch_pdl(kern, dim3(a.hq, a.num_seqs), dim3(kDecD), 0, a.stream, "decode combine launch",
+                    p);
 }
 
 int launch_paged_decode(const AttnArgs& a) {
@@ -434,29 +295,27 @@ int launch_paged_decode(const AttnArgs& a) {
     p.ws_o = reinterpret_cast<float*>(a.ws);
     p.ws_lse = p.ws_o + n * kDecD;
   }
+#ifdef NVKV_DECODE_SPLIT_MAJOR
+  dim3 grid(a.num_seqs, a.hkv, splits);
+#else
   dim3 grid(splits, a.hkv, a.num_seqs);
+#endif
   if (a.dtype == NVKV_DTYPE_BF16) {
     auto kern = paged_decode_kernel<__nv_bfloat16>;
     static unsigned long long attr_done_1 = 0;
     rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_1);
-    if (rc) return rc;
-    kern<<<grid, kDecThreads, kDecSmemBytes, a.stream>>>(mk, mv, p);
-    if (splits > 1) {
-      rc = launch_combine(decode_combine_kernel<__nv_bfloat16>, p, a);
-      if (rc) return rc;
-    }
+    if (!rc) rc = launch_pdl(kern, grid, dim3(kDecThreads), kDecSmemBytes, a.stream,
+                             "paged decode launch", mk, mv, p);
+    if (!rc && splits > 1) rc = launch_combine(decode_combine_kernel<__nv_bfloat16>, p, a);
   } else {
     auto kern = paged_decode_kernel<__half>;
     static unsigned long long attr_done_2 = 0;
     rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_2);
-    if (rc) return rc;
-    kern<<<grid, kDecThreads, kDecSmemBytes, a.stream>>>(mk, mv, p);
-    if (splits > 1) {
-      rc = launch_combine(decode_combine_kernel<__half>, p, a);
-      if (rc) return rc;
-    }
+    if (!rc) rc = launch_pdl(kern, grid, dim3(kDecThreads), kDecSmemBytes, a.stream,
+                             "paged decode launch", mk, mv, p);
+    if (!rc && splits > 1) rc = launch_combine(decode_combine_kernel<__half>, p, a);
   }
-  return check_cuda(cudaGetLastError(), "paged decode launch");
+  return rc;
 }
 
 }  // namespace nvkv

@@ -166,3 +166,63 @@ def test_decode_graph_replays_reuse_the_merge_counters():
         torch.cuda.synchronize()
         assert_attention_close(out, _oracle(q, kc, vc, tables, lens), "replay")
     graph.reset()
+
+
+def test_decode_large_batch():
+    """1100 sequences of up to 3000 keys (a grid of 2200 work items); checked
+    on every 37th sequence."""
+    rng = np.random.default_rng(11)
+    lens = rng.integers(1, 3000, 1100).tolist()
+    _decode_case(lens, 8, 2, seed=11, check=range(0, 1100, 37))
+
+
+def test_decode_ragged_tiny_batch():
+    """Ragged tiny batches: most keys in partial tiles, single-tile and
+    one-key sequences next to multi-tile ones."""
+    _decode_case([1, 65, 3, 200, 64, 1], 16, 2, seed=12)
+    _decode_case([130], 4, 1, seed=13)
+
+
+def test_decode_two_long_sequences_one_kv_head():
+    """Two long sequences at one kv head: the plan splits each ~150 ways."""
+    _decode_case([20000, 17001], 8, 1, seed=14)
+
+
+def test_decode_empty_context_writes_zeros_and_reports():
+    """A decode row with k_len == 0 (no keys): zeros plus DEVERR_SEQLEN, the
+    other rows unaffected (a small batch that splits and a large one that
+    does not)."""
+    for B in (3, 1030):
+        g = torch.Generator().manual_seed(15)
+        lens = [0] + [100] * (B - 1)
+        nb = B + 2
+        kc, vc, bt, tables = make_paged([max(L, 1) for L in lens], 256, 2, 128, nb, g)
+        q = torch.randn(B, 4, 128, generator=g).to(torch.bfloat16).cuda()
+        nvkv.device_error()
+        out = nvkv.paged_attention(q, kc, vc, cu([1] * B), cu(lens), torch.from_numpy(
+            bt.view(np.int32)).cuda(), 1, 100, 0.1)
+        torch.cuda.synchronize()
+        assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
+        assert torch.count_nonzero(out[0]) == 0
+        kb, vb = gather_seq(kc, vc, tables[1], 100)
+        assert_attention_close(out[1:2], O.causal_attention_one(f32(q)[1:2], kb, vb, 0.1), "row 1")
+
+
+def test_decode_repeated_calls_are_bitwise_identical():
+    """Three calls on the 8B TP8 decode shape with one workspace: the
+    split-KV plan and every reduction order are fixed, so the outputs are
+    bit-identical (and match the oracle)."""
+    rng = np.random.default_rng(21)
+    lens = rng.integers(1025, 1537, 256).tolist()
+    q, kc, vc, bt, tables = _split_case(lens, 4, 1, 21)
+    ws = torch.zeros(nvkv.workspace_size(len(lens), 4, 1, 1, max(lens)), dtype=torch.uint8,
+                     device="cuda")
+    run = lambda: nvkv.paged_attention(q, kc, vc, cu([1] * len(lens)), cu(lens), bt, 1,  # noqa
+                                       max(lens), 128 ** -0.5, workspace=ws)
+    outs = [run() for _ in range(3)]
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    sub = list(range(0, 256, 16))
+    want = _oracle(q[sub], kc, vc, [tables[b] for b in sub], [lens[b] for b in sub])
+    assert_attention_close(outs[2][sub], want, "repeat")
