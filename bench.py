@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nvkv", choices=["nvkv", "reference"])
     ap.add_argument("--no-graph", action="store_true", help="eager launches (no CUDA graph)")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="tp > 1: NCCL all-reduce + nvkv_rms_norm instead of the fused "
+                         "peer-memory nvkv_allreduce_rms_norm")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -180,6 +183,79 @@ def _barrier(world):
     torch.cuda.synchronize()
 
 
+def _allreduce_bw(world, dev, nbytes, reps=50):
+    """NCCL all-reduce of the step's own message (T x hidden bf16), `reps`
+    calls captured in one CUDA graph as in the step, timed with CUDA events,
+    max over ranks.  Bus bandwidth as nccl-tests defines it:
+    algbw * 2 (n - 1) / n."""
+    import torch
+    import torch.distributed as dist
+    x = torch.zeros(nbytes // 2, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        dist.all_reduce(x)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            dist.all_reduce(x)
+    g.replay()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / reps
+    g.reset()  # a graph holding NCCL calls must go before the process group
+    torch.cuda.synchronize()
+    algbw = nbytes / (ms * 1e-3) / 1e9
+    return ms, algbw, algbw * 2 * (world - 1) / world
+
+
+def _peer_allreduce_bw(model, world, dev, T, reps=50):
+    """The fused nvkv_allreduce_rms_norm on the step's shape (T x hidden bf16),
+    `reps` calls in one CUDA graph, CUDA events, max over ranks; bus bandwidth
+    on the all-reduce's bytes as for NCCL."""
+    import torch
+    H = model.cfg.hidden_size
+    res = torch.zeros(T, H, dtype=model.dtype, device=dev)
+    out = torch.empty_like(res)
+    w = model.norm
+    model.comm.input(T, H, model.dtype).zero_()
+    for _ in range(3):
+        model.comm.allreduce_rms_norm(T, H, res, w, 1e-6, out)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        model.comm.allreduce_rms_norm(T, H, res, w, 1e-6, out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            model.comm.allreduce_rms_norm(T, H, res, w, 1e-6, out)
+    g.replay()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / reps
+    g.reset()
+    torch.cuda.synchronize()
+    nbytes = T * H * 2
+    algbw = nbytes / (ms * 1e-3) / 1e9
+    return ms, algbw, algbw * 2 * (world - 1) / world
+
+
 def run_nvkv(a):
     import torch
 
@@ -193,7 +269,8 @@ def run_nvkv(a):
         from dataclasses import replace
         cfg = replace(cfg, num_hidden_layers=a.layers)
     w = workload()
-    model = Qwen3TP(cfg, rank, world, seed=0, device=dev)
+    model = Qwen3TP(cfg, rank, world, seed=0, device=dev,
+                    peer_allreduce=not a.nccl_allreduce, max_tokens=NUM_SEQS)
     model.allocate_kv_cache(w["num_blocks"], PAGE, fill_random=True)
     host = {k: torch.from_numpy(np.ascontiguousarray(w[k])).pin_memory()
             for k in ("input_ids", "positions", "slot_mapping", "cu_q", "cu_k", "block_tables")}
@@ -203,7 +280,7 @@ def run_nvkv(a):
     tok_host = torch.empty(NUM_SEQS, dtype=torch.int64).pin_memory()
 
     def step_fn():
-        return model.forward(st).argmax(-1)
+        return model.greedy(st)
 
     for _ in range(max(1, a.warmup)):
         tok = step_fn()
@@ -279,6 +356,26 @@ def run_nvkv(a):
     kern_ms = _max_over_ranks(kern_ms, world, dev)
     assert nvkv.device_error() == 0
     launches = model.launches_per_step(st) * a.steps
+    ar = None
+    if world > 1:  # every rank takes this step, in the same order
+        ar_bytes = NUM_SEQS * cfg.hidden_size * 2
+        ar_ms, ar_alg, ar_bus = _allreduce_bw(world, dev, ar_bytes)
+        per_step = 2 * cfg.num_hidden_layers + 1
+        ar = {"op": "all_reduce (o_proj, down_proj, embedding)", "bytes": ar_bytes,
+              "us_per_call": round(ar_ms * 1e3, 2), "calls_per_step": per_step,
+              "algbw_gbs": round(ar_alg, 1), "busbw_gbs": round(ar_bus, 1),
+              "peak_gbs": 900.0, "peak_source": "NVLink 5 nominal per direction",
+              "frac": round(ar_bus / 900.0, 4),
+              "share_of_step": round(per_step * ar_ms / (ms / a.steps), 4),
+              "step_route": "nccl all_reduce + nvkv_rms_norm" if model.comm is None else
+                            "nvkv_allreduce_rms_norm (peer memory)"}
+        if model.comm is not None:
+            pm, pa, pb = _peer_allreduce_bw(model, world, dev, NUM_SEQS)
+            ar["fused"] = {"op": "nvkv_allreduce_rms_norm (all-reduce + residual + RMSNorm, "
+                                 "NVLink peer loads/stores)",
+                           "us_per_call": round(pm * 1e3, 2), "algbw_gbs": round(pa, 1),
+                           "busbw_gbs": round(pb, 1), "frac": round(pb / 900.0, 4),
+                           "share_of_step": round(per_step * pm / (ms / a.steps), 4)}
 
     if rank == 0:
         peak, peak_kind = load_peak()
@@ -292,7 +389,7 @@ def run_nvkv(a):
             "data": "synthetic (seeded random-init weights, random prefilled KV, random token ids)",
             "config": {
                 "workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256, all 36 "
-                            "layers + lm_head + argmax; attention path = nvkv kernels, GEMMs = "
+                            "layers + lm_head + vocab-parallel argmax; attention path = nvkv kernels, GEMMs = "
                             "cuBLAS, TP collectives = NCCL",
                 "model": "Qwen3-8B", "global_batch": NUM_SEQS, "seq_len": int(w["max_k"]),
                 "parallelism": f"tp{world}", "cuda_graph": graph is not None,
@@ -310,6 +407,8 @@ def run_nvkv(a):
                                            "shape, scaled to this launch's algorithmic bytes"},
             "clocks": clocks,
         }
+        if ar is not None:
+            line["collectives"] = ar
         if world == 1:
             line["cpu_baseline"] = cpu_reference(max_seconds=20.0)
         print(json.dumps(line), flush=True)
@@ -329,7 +428,8 @@ def run_nvkv(a):
             os._exit(0)
 
         threading.Thread(target=_exit_if_stuck, daemon=True).start()
-        dist.barrier()
+        dist.barrier()  # every rank's last peer-memory call has completed
+        model.close()
         dist.destroy_process_group()
 
 

@@ -208,6 +208,65 @@ int nvkv_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, in
                       int64_t num_tokens, int inter, int dtype, nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Tensor-parallel epilogue: all-reduce of the row-parallel partial sums,
+ * residual add and RMSNorm in ONE kernel over NVLink peer memory.
+ *
+ * Replaces, at each all-reduce of the decoder, the NCCL call of
+ * RowParallelLinear::forward (layers/linear.rs:200-208) and of
+ * VocabParallelEmbedding::forward (layers/embed_head.rs:58), made through
+ * AllReduce (layers/dist_util.rs:29-84), together with the
+ * RMSNorm::forward / residual_forward (layers/layernorm.rs:18-42) that
+ * follows every one of them in Qwen3 (models/qwen3.rs:232-238, 295).
+ *
+ * One process per GPU.  Every rank creates a communicator (one device
+ * allocation holding an input buffer, a gather buffer and barrier flags),
+ * passes its NVKV_COMM_HANDLE_BYTES handle to every other rank over any
+ * out-of-band channel (an all-gather on the process group), and opens the
+ * peers' allocations (cudaIpcOpenMemHandle).  The producer of the partial
+ * sums (the o_proj / down_proj GEMM, the masked embedding lookup) writes
+ * them into the buffer nvkv_comm_input returns, [num_tokens, hidden]
+ * contiguous; then every rank calls nvkv_allreduce_rms_norm with the same
+ * num_tokens and hidden, in the same order:
+ *   s = sum over ranks of input (f32, rank order, rounded once to dtype)
+ *   NVKV_RESIDUAL_ADD:  r = dtype(s + residual), y = rms_norm(s + residual)
+ *   NVKV_RESIDUAL_INIT: r = s,                   y = rms_norm(s)
+ * (rounding points of nvkv_rms_norm), residual and out [num_tokens, hidden]
+ * contiguous, identical on every rank.  Each rank reduces its 1/world share
+ * of the tokens with peer loads and writes the result into every rank's
+ * gather buffer with peer stores; flags in peer memory order the phases.
+ * Barrier epochs live on the device, so calls may be captured in a CUDA
+ * graph and replayed.  A wait that exceeds the communicator's timeout
+ * (2 s by default) records NVKV_DEVERR_PEER_TIMEOUT and the kernel returns;
+ * the communicator must then be destroyed and recreated on every rank.
+ * world <= NVKV_COMM_MAX_RANKS, hidden % 8 == 0, hidden <= 8192,
+ * num_tokens * hidden * 2 <= max_bytes.  Destroy only after every rank's last
+ * call has completed (e.g. after a barrier).  No counterpart in the
+ * reference for the fusion itself: there the all-reduce is an NCCL call.
+ * ---------------------------------------------------------------------- */
+#define NVKV_COMM_HANDLE_BYTES 64
+#define NVKV_COMM_MAX_RANKS 8
+#define NVKV_DEVERR_PEER_TIMEOUT 5    /* a peer missed a barrier of the comm */
+#define NVKV_RESIDUAL_ADD 0
+#define NVKV_RESIDUAL_INIT 1
+
+typedef struct nvkv_comm* nvkv_comm_t;
+
+/* Allocates this rank's buffers (zeroed flags) on the current device and
+ * writes its handle (NVKV_COMM_HANDLE_BYTES) to handle_out. */
+int nvkv_comm_create(int rank, int world, size_t max_bytes, nvkv_comm_t* out, void* handle_out);
+/* handles: world * NVKV_COMM_HANDLE_BYTES, in rank order (this rank's own
+ * entry is ignored).  Call once, before the first all-reduce. */
+int nvkv_comm_open_peers(nvkv_comm_t comm, const void* handles);
+/* Device address of this rank's input buffer (max_bytes). */
+int nvkv_comm_input(nvkv_comm_t comm, void** ptr);
+/* Barrier wait limit in nanoseconds (> 0). */
+int nvkv_comm_set_timeout(nvkv_comm_t comm, int64_t timeout_ns);
+int nvkv_comm_destroy(nvkv_comm_t comm);
+int nvkv_allreduce_rms_norm(nvkv_comm_t comm, int64_t num_tokens, int hidden, void* residual,
+                            int residual_mode, const void* weight, float eps, void* out,
+                            int dtype, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Host-side mirror of the reference's operator surface, for callers that
  * drive the path the way nanovllm_rs's Attention does: a per-thread Context
  * (utils/context.rs:4-54) published once per step, and an Attention object

@@ -12,79 +12,18 @@
 // Layout: one CTA (256 threads) per token row for the norm, every thread
 // holding up to 32 elements in registers (16-byte loads), a block reduction of
 // the f32 sum of squares; a grid-stride 16-byte loop for SiLU*mul.
-#include "common.cuh"
+#include "norm_row.cuh"
 
 namespace nvkv {
 
-constexpr int kNormThreads = 256;
-constexpr int kNormMaxVec = 4;  // 8-element vectors per thread: H <= 256 * 8 * 4 = 8192
-
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(
-    const T* __restrict__ x, int64_t x_stride, T* __restrict__ residual,
-    int64_t res_stride, const T* __restrict__ w, float eps, T* __restrict__ out,
-    int64_t out_stride, int H) {
+    const T* __restrict__ x, int64_t x_stride, T* residual, int64_t res_stride,
+    const T* __restrict__ w, float eps, T* __restrict__ out, int64_t out_stride, int H) {
   __shared__ float red[kNormThreads / 32];
   const int64_t t = blockIdx.x;
-  const int tid = threadIdx.x;
-  const int nvec = H / 8;
-  float v[kNormMaxVec][8];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
-    const int c = tid + i * kNormThreads;
-    if (c < nvec) {
-      const uint4 a = *reinterpret_cast<const uint4*>(x + t * x_stride + c * 8);
-      const uint32_t* ap = reinterpret_cast<const uint32_t*>(&a);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = DT<T>::to_f2(ap[e]);
-        v[i][2 * e] = f.x;
-        v[i][2 * e + 1] = f.y;
-      }
-      if (residual) {
-        const uint4 b = *reinterpret_cast<const uint4*>(residual + t * res_stride + c * 8);
-        const uint32_t* bp = reinterpret_cast<const uint32_t*>(&b);
-        uint4 nr;
-        uint32_t* np = reinterpret_cast<uint32_t*>(&nr);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = DT<T>::to_f2(bp[e]);
-          v[i][2 * e] += f.x;
-          v[i][2 * e + 1] += f.y;
-          np[e] = DT<T>::from_f2(v[i][2 * e], v[i][2 * e + 1]);
-        }
-        *reinterpret_cast<uint4*>(residual + t * res_stride + c * 8) = nr;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += __fmul_rn(v[i][e], v[i][e]);  // rounded squares (x.sqr())
-    }
-  }
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-  if ((tid & 31) == 0) red[tid >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
-  const float inv = 1.0f / sqrtf(tot * (1.0f / (float)H) + eps);  // mean = sum * (1/H)
-#pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
-    const int c = tid + i * kNormThreads;
-    if (c < nvec) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(w + c * 8);
-      const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wv);
-      uint4 o;
-      uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 wf = DT<T>::to_f2(wp[e]);
-        op[e] = DT<T>::from_f2(rnd<T>(v[i][2 * e] * inv) * wf.x,
-                               rnd<T>(v[i][2 * e + 1] * inv) * wf.y);
-      }
-      *reinterpret_cast<uint4*>(out + t * out_stride + c * 8) = o;
-    }
-  }
+  T* r = residual ? residual + t * res_stride : nullptr;
+  norm_row<T>(x + t * x_stride, r, r, w, eps, out + t * out_stride, H, red);
 }
 
 template <typename T>

@@ -29,6 +29,12 @@ DEVERR_SLOT_RANGE = 1
 DEVERR_BLOCK_RANGE = 2
 DEVERR_POSITION_RANGE = 3
 DEVERR_SEQLEN = 4
+DEVERR_PEER_TIMEOUT = 5
+
+COMM_HANDLE_BYTES = 64
+COMM_MAX_RANKS = 8
+RESIDUAL_ADD = 0
+RESIDUAL_INIT = 1
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -53,6 +59,12 @@ SIGNATURES = {
                                      _p],
     "nvkv_rms_norm": [_p, _i64, _p, _i64, _p, _f32, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_silu_and_mul": [_p, _i64, _p, _i64, _i64, _i32, _i32, _p],
+    "nvkv_comm_create": [_i32, _i32, _sz, ctypes.POINTER(_p), _p],
+    "nvkv_comm_open_peers": [_p, _p],
+    "nvkv_comm_input": [_p, ctypes.POINTER(_p)],
+    "nvkv_comm_set_timeout": [_p, _i64],
+    "nvkv_comm_destroy": [_p],
+    "nvkv_allreduce_rms_norm": [_p, _i64, _i32, _p, _i32, _p, _f32, _p, _i32, _p],
     "nvkv_context_set": [_p, _p, _i32, _i32, _i32, _p, _i64, _p, _p, _i64],
     "nvkv_context_reset": [],
     "nvkv_attention_create": [_f32, ctypes.POINTER(_p)],

@@ -2,12 +2,15 @@
 
 This is the caller side of the path (models/qwen3.rs:126-146,179-183,226-297,
 layers/linear.rs, layers/embed_head.rs) restated with torch for everything
-that is NOT one of the path's kernels: the projections are cuBLAS GEMMs and
-the tensor-parallel collectives are NCCL through torch.distributed.  Per layer
-the attention hot path is two nvkv launches, nvkv_qknorm_rope (split_qkv +
-q/k RMSNorm + RoPE + KV-cache store, fused) and nvkv_paged_attention
-(split-KV decode or tcgen05 prefill), and the epilogues around it are nvkv's
-fused residual RMSNorm (x2) and SiLU*mul.
+that is NOT one of the path's kernels: the projections are cuBLAS GEMMs.  Per
+layer the attention hot path is two nvkv launches, nvkv_qknorm_rope
+(split_qkv + q/k RMSNorm + RoPE + KV-cache store, fused) and
+nvkv_paged_attention (split-KV decode or tcgen05 prefill), and the epilogues
+around it are nvkv's fused residual RMSNorm (x2) and SiLU*mul.  At tp > 1
+each all-reduce and the RMSNorm after it are one nvkv kernel over NVLink
+peer memory (nvkv_allreduce_rms_norm); with peer_allreduce=False they are an
+NCCL all-reduce (torch.distributed) followed by nvkv_rms_norm.  The greedy
+pick and the logit all-gather stay on torch.distributed.
 
 Tensor-parallel layout (one process per GPU), as the reference shards it:
   * qkv_proj   column-parallel, local rows [q_r ; k_r ; v_r]  (linear.rs:214-281)
@@ -114,6 +117,27 @@ def gather_logits(local: torch.Tensor, group=None) -> torch.Tensor:
     return torch.cat(parts, dim=-1)
 
 
+def vocab_parallel_argmax(local: torch.Tensor, rank: int, group=None) -> torch.Tensor:
+    """Greedy token of vocab-sharded logits without gathering them: each rank
+    takes its shard's max and first arg-max, one (value, global index) pair per
+    row is all-gathered, and the largest value wins, ties going to the lowest
+    index -- exactly argmax over the concatenated logits (gather_logits) at
+    T x 16 bytes per rank instead of T x V/tp x 4."""
+    v, i = local.max(dim=-1)
+    gi = i + rank * local.size(-1)
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return gi
+    ws = dist.get_world_size(group)
+    pair = torch.stack([v.double(), gi.double()], dim=-1)
+    parts = [torch.empty_like(pair) for _ in range(ws)]
+    dist.all_gather(parts, pair, group=group)
+    allp = torch.stack(parts, 0)  # [ws, T, 2]
+    vals, idx = allp[..., 0], allp[..., 1]
+    best = vals.max(0).values
+    pick = torch.where(vals == best, idx, torch.full_like(idx, float("inf"))).min(0).values
+    return pick.long()
+
+
 # ---------------------------------------------------------------------------
 # Step metadata on the device (what ModelRunner::prepare_model_input uploads)
 # ---------------------------------------------------------------------------
@@ -136,7 +160,12 @@ class Qwen3TP:
 
     def __init__(self, cfg: Qwen3Config, rank: int = 0, tp: int = 1, seed: int = 0,
                  dtype=torch.bfloat16, device="cuda", init_scale: float = 1.0, group=None,
-                 embed_std: float = 1.0, head_std: Optional[float] = None):
+                 embed_std: float = 1.0, head_std: Optional[float] = None,
+                 peer_allreduce: bool = True, max_tokens: int = 4096):
+        """peer_allreduce (tp > 1): every all-reduce + the RMSNorm after it is one
+        nvkv kernel over NVLink peer memory (nvkv.comm.PeerComm) instead of an
+        NCCL call followed by nvkv_rms_norm; max_tokens bounds the tokens of a
+        step on that route."""
         self.cfg, self.rank, self.tp, self.group = cfg, rank, tp, group
         self.dtype, self.device = dtype, torch.device(device)
         self.hq = divide(cfg.num_attention_heads, tp)
@@ -185,6 +214,17 @@ class Qwen3TP:
         self.k_caches: List[torch.Tensor] = []
         self.v_caches: List[torch.Tensor] = []
         self._bufs = {}
+        self.comm = None
+        if tp > 1 and peer_allreduce:
+            from .comm import PeerComm
+            self.comm = PeerComm(rank, tp, max_tokens * H * torch.tensor([], dtype=dtype)
+                                 .element_size(), group=group)
+
+    def close(self) -> None:
+        """Releases the peer communicator (after every rank's last step)."""
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     # ---- KV pool (model_runner.rs:286-303): per layer [Nb, P, Hkv/tp, D] ----
     def allocate_kv_cache(self, num_blocks: int, block_size: int = 256, fill_random: bool = False,
@@ -219,6 +259,18 @@ class Qwen3TP:
         """Qwen3ForCausalLM::forward + compute_logits (qwen3.rs:285-297,
         embed_head.rs:89-119): returns the full-vocab logits of each
         sequence's last token, [B, V] (float32)."""
+        return gather_logits(self._local_logits(st), self.group)
+
+    @torch.no_grad()
+    def greedy(self, st: Step) -> torch.Tensor:
+        """The greedy next token of every sequence, [B] int64: argmax of
+        forward()'s logits, taken vocab-parallel (vocab_parallel_argmax)."""
+        return vocab_parallel_argmax(self._local_logits(st), self.rank, self.group)
+
+    def _local_logits(self, st: Step) -> torch.Tensor:
+        """This rank's vocab shard of the last-token logits, [B, V/tp] float32."""
+        if self.comm is not None:
+            return self._local_logits_peer(st)
         cfg = self.cfg
         T = st.input_ids.numel()
         D = cfg.head_dim
@@ -256,14 +308,61 @@ class Qwen3TP:
         last = h.index_select(0, st.last_idx)
         # bf16 operands, fp32 output: no bf16 rounding of the logits, so the
         # greedy argmax sees no artificial ties
-        logits = torch.mm(last, self.lm_head.t(), out_dtype=torch.float32)
-        return gather_logits(logits, self.group)
+        return torch.mm(last, self.lm_head.t(), out_dtype=torch.float32)
+
+    def _local_logits_peer(self, st: Step) -> torch.Tensor:
+        """_local_logits with every all-reduce fused into the RMSNorm after it:
+        the producers (masked embedding lookup, o_proj, down_proj) write their
+        partial sums into the communicator's input buffer, and one kernel
+        all-reduces them, updates the residual and normalises
+        (qwen3.rs:232-238, 295)."""
+        cfg = self.cfg
+        T = st.input_ids.numel()
+        D = cfg.head_dim
+        H = cfg.hidden_size
+        eps = cfg.rms_norm_eps
+        part = self.comm.input(T, H, self.dtype)
+        q_buf = self._buf("q", (T, self.hq, D))
+        o_buf = self._buf("o", (T, self.hq, D))
+        ws_n = ops.workspace_size(st.cu_seqlens_q.numel() - 1, self.hq, self.hkv, st.max_seqlen_q,
+                                  st.max_seqlen_k, D)
+        ws = self._buf("ws", (max(ws_n, 16),), torch.uint8)
+        xb = self._buf("x", (T, H))
+        res = self._buf("res", (T, H))
+        actb = self._buf("act", (T, self.ffn))
+        # embed_head.rs:47-60 without its all-reduce: the masked local lookup
+        n = self.embed.size(0)
+        start = self.rank * n
+        mask = (st.input_ids >= start) & (st.input_ids < start + n)
+        torch.mul(torch.nn.functional.embedding((st.input_ids - start) * mask, self.embed),
+                  mask.unsqueeze(-1), out=part)
+        self.comm.allreduce_rms_norm(T, H, res, self.layers[0]["ln1"], eps, xb, init=True)
+        for li, L in enumerate(self.layers):
+            qkv = torch.matmul(xb, L["qkv"].t())
+            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"], eps,
+                            cfg.rope_theta, cfg.max_position_embeddings, D,
+                            k_cache=self.k_caches[li], v_cache=self.v_caches[li],
+                            slot_mapping=st.slot_mapping, q_out=q_buf)
+            ops.paged_attention(q_buf, self.k_caches[li], self.v_caches[li], st.cu_seqlens_q,
+                                st.cu_seqlens_k, st.block_tables, st.max_seqlen_q,
+                                st.max_seqlen_k, self.scale, out=o_buf, workspace=ws)
+            torch.matmul(o_buf.view(T, -1), L["o"].t(), out=part)
+            self.comm.allreduce_rms_norm(T, H, res, L["ln2"], eps, xb)
+            gu = torch.matmul(xb, L["gate_up"].t())
+            act = ops.silu_and_mul(gu, out=actb)
+            torch.matmul(act, L["down"].t(), out=part)
+            nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.norm
+            self.comm.allreduce_rms_norm(T, H, res, nxt, eps, xb)
+        last = xb.index_select(0, st.last_idx)
+        return torch.mm(last, self.lm_head.t(), out_dtype=torch.float32)
 
     def launches_per_step(self, st: Step) -> int:
-        """nvkv kernel launches one forward issues: per layer two RMSNorms,
-        SiLU*mul, the prologue, the decode kernel, the combine kernel when the
-        split-KV plan splits, and the prefill kernel when any sequence has
-        q_len > 1; plus the final norm."""
+        """nvkv kernel launches one forward issues: per layer two RMSNorms
+        (each fused with the all-reduce before it on the peer route), SiLU*mul,
+        the prologue, the decode kernel, the combine kernel when the split-KV
+        plan splits, and the prefill kernel when any sequence has q_len > 1;
+        plus the final norm (on the peer route: the embedding's fused call,
+        the final norm being fused into the last layer's)."""
         B = st.cu_seqlens_q.numel() - 1
         split = ops.workspace_size(B, self.hq, self.hkv, st.max_seqlen_q, st.max_seqlen_k) > 0
         per = 5 + (1 if split else 0) + (1 if st.max_seqlen_q > 1 else 0)

@@ -115,3 +115,20 @@ def test_qknorm_validation():
     assert call(kc=p) == ERR_INVALID_ARG  # cache without v_cache / slot_mapping
     assert call(stride=100) == ERR_INVALID_ARG
     assert call(qkv=ctypes.c_void_p((1 << 20) + 2)) == ERR_ALIGNMENT
+
+
+def test_comm_validation_host_only():
+    """nvkv_comm_* / nvkv_allreduce_rms_norm reject bad arguments before any
+    device call."""
+    from nvkv._lib import lib, ERR_INVALID_ARG, OK
+    h = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(64)
+    assert lib.nvkv_comm_create(2, 2, 1 << 20, ctypes.byref(h), buf) == ERR_INVALID_ARG
+    assert lib.nvkv_comm_create(0, 9, 1 << 20, ctypes.byref(h), buf) == ERR_INVALID_ARG
+    assert lib.nvkv_comm_create(0, 2, 0, ctypes.byref(h), buf) == ERR_INVALID_ARG
+    assert lib.nvkv_comm_create(0, 2, 1 << 20, None, buf) == ERR_INVALID_ARG
+    assert b"rank" in lib.nvkv_last_error() or b"null" in lib.nvkv_last_error()
+    assert lib.nvkv_allreduce_rms_norm(None, 4, 4096, None, 0, None, 1e-6, None, 1,
+                                       None) == ERR_INVALID_ARG
+    assert lib.nvkv_comm_set_timeout(None, 1) == ERR_INVALID_ARG
+    assert lib.nvkv_comm_destroy(None) == OK

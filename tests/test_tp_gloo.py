@@ -24,7 +24,7 @@ def _worker(rank, world, port, q):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world)
         from nvkv.decoder import (gather_logits, shard_merged, shard_qkv, shard_row, shard_vocab,
-                                  vocab_parallel_embed)
+                                  vocab_parallel_argmax, vocab_parallel_embed)
         g = torch.Generator().manual_seed(0)
         H, hq, hkv, D, F, V, T = 64, 4, 2, 8, 48, 40, 5
         x = torch.randn(T, H, generator=g, dtype=torch.float64)
@@ -63,6 +63,14 @@ def _worker(rank, world, port, q):
         # vocab-parallel lm_head: local logits + all-gather concat (embed_head.rs:113-117)
         lg = gather_logits(x @ shard_vocab(emb, rank, world).T)
         assert torch.allclose(lg, x @ emb.T)
+        # vocab-parallel greedy pick == argmax of the gathered logits, also on
+        # ties inside a shard and across the shard boundary (first index wins)
+        full = (x @ emb.T).float()
+        full[1, 3] = full[1, 30] = full[1].max() + 1.0   # tie across shards
+        full[2, 25] = full[2, 27] = full[2].max() + 1.0  # tie inside shard 1
+        full[3, :] = 0.5                                  # all equal
+        local = full[:, rank * (V // world):(rank + 1) * (V // world)]
+        assert torch.equal(vocab_parallel_argmax(local, rank), full.argmax(-1))
         q.put((rank, "ok"))
     except Exception as ex:  # pragma: no cover - reported to the parent
         q.put((rank, repr(ex)))
