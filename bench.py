@@ -335,24 +335,41 @@ def run_nvkv(a):
     ms_e2e = _max_over_ranks(e0.elapsed_time(e1), world, dev)
     _barrier(world)
 
-    # ---- roofline: per-launch CUDA events around the decode attention of every layer ----
+    # ---- roofline: the decode attention of every layer, graph-replayed ----
+    # The 36 layers' paged-attention calls (decode kernel + split-KV combine,
+    # same inputs as the step) are captured in one CUDA graph, as in the step,
+    # so no host launch gap sits between them; `reps` replays between two CUDA
+    # events on this stream give the mean device time per call.
     q = model._bufs["q"]
     o = model._bufs["o"]
     ws = model._bufs["ws"]
     reps = max(3, min(a.steps, 20))
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(reps * cfg.num_hidden_layers)]
-    i = 0
-    for _ in range(reps):
+
+    def attn_all_layers():
         for li in range(cfg.num_hidden_layers):
-            evs[i][0].record()
             ops.paged_attention(q, model.k_caches[li], model.v_caches[li], st.cu_seqlens_q,
                                 st.cu_seqlens_k, st.block_tables, 1, w["max_k"], model.scale,
                                 out=o, workspace=ws)
-            evs[i][1].record()
-            i += 1
+
+    attn_all_layers()
     torch.cuda.synchronize()
-    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in evs)
+    s_side = torch.cuda.Stream()
+    s_side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s_side):
+        attn_all_layers()
+    torch.cuda.current_stream().wait_stream(s_side)
+    agraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(agraph):
+        attn_all_layers()
+    agraph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        agraph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    kern_ms = e0.elapsed_time(e1) / (reps * cfg.num_hidden_layers)
+    agraph.reset()
     kern_ms = _max_over_ranks(kern_ms, world, dev)
     assert nvkv.device_error() == 0
     launches = model.launches_per_step(st) * a.steps
@@ -390,9 +407,13 @@ def run_nvkv(a):
             "config": {
                 "workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256, all 36 "
                             "layers + lm_head + vocab-parallel argmax; attention path = nvkv kernels, GEMMs = "
-                            "cuBLAS, TP collectives = NCCL",
+                            "cuBLAS, TP all-reduce + RMSNorm = nvkv peer-memory kernel (NCCL "
+                            "with --nccl-allreduce), greedy-pick all-gather = NCCL",
                 "model": "Qwen3-8B", "global_batch": NUM_SEQS, "seq_len": int(w["max_k"]),
                 "parallelism": f"tp{world}", "cuda_graph": graph is not None,
+                "allreduce_route": ("none" if world == 1 else
+                                    "nccl + nvkv_rms_norm" if model.comm is None else
+                                    "nvkv_allreduce_rms_norm"),
                 "l2": "inputs larger than L2 (per-step KV read >> 126 MB), no flush",
             },
             "e2e": {"value": round(NUM_SEQS * a.steps / (ms_e2e * 1e-3), 1), "unit": "tok/s",
