@@ -61,7 +61,10 @@ struct DecState {
 // S = Q.K^T (two n8 key tiles), fp32 online softmax with quad shuffles, then
 // O += P.V with P re-packed from the S accumulators as the A operand and
 // the V fragments of missing keys zeroed (stale cache rows never reach O).
-template <typename T>
+// kHi = false (group size <= 8): rows 8..15 (r1) are padding, so their
+// softmax is skipped and their P rows are zero -- half of the exp2 and
+// conversion work (the XU pipe) -- while the MMAs stay as they are.
+template <typename T, bool kHi>
 __device__ __forceinline__ void dec_tile(const uint32_t (&qa)[8][4], DecState& st, uint32_t kbase,
                                          uint32_t vbase, int wtok, int valid, float scale_log2,
                                          int lane) {
@@ -90,46 +93,58 @@ __device__ __forceinline__ void dec_tile(const uint32_t (&qa)[8][4], DecState& s
     for (int e = 0; e < 2; ++e) {
       const bool ok = (nt * 8 + cq + e) < valid;
       sc[nt][e] = ok ? sc[nt][e] * scale_log2 : -INFINITY;
-      sc[nt][e + 2] = ok ? sc[nt][e + 2] * scale_log2 : -INFINITY;
       mx0 = fmaxf(mx0, sc[nt][e]);
-      mx1 = fmaxf(mx1, sc[nt][e + 2]);
+      if (kHi) {
+        sc[nt][e + 2] = ok ? sc[nt][e + 2] * scale_log2 : -INFINITY;
+        mx1 = fmaxf(mx1, sc[nt][e + 2]);
+      }
     }
   }
   mx0 = warp_max_xor(warp_max_xor(mx0, 1), 2);
-  mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
-  const float mn0 = fmaxf(st.m0, mx0), mn1 = fmaxf(st.m1, mx1);
+  const float mn0 = fmaxf(st.m0, mx0);
   const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
-  const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-  const float al0 = exp2f(st.m0 - mu0), al1 = exp2f(st.m1 - mu1);
+  const float al0 = exp2f(st.m0 - mu0);
   st.m0 = mn0;
-  st.m1 = mn1;
-  float ps0 = 0.f, ps1 = 0.f;
+  float al1 = 1.f;
+  if (kHi) {
+    mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
+    const float mn1 = fmaxf(st.m1, mx1);
+    const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+    al1 = exp2f(st.m1 - mu1);
+    st.m1 = mn1;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      sc[nt][2] = exp2f(sc[nt][2] - mu1);
+      sc[nt][3] = exp2f(sc[nt][3] - mu1);
+    }
+    st.l1 = st.l1 * al1 + (sc[0][2] + sc[0][3] + sc[1][2] + sc[1][3]);
+  }
+  float ps0 = 0.f;
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       sc[nt][e] = exp2f(sc[nt][e] - mu0);
-      sc[nt][e + 2] = exp2f(sc[nt][e + 2] - mu1);
       ps0 += sc[nt][e];
-      ps1 += sc[nt][e + 2];
     }
   }
   st.l0 = st.l0 * al0 + ps0;
-  st.l1 = st.l1 * al1 + ps1;
   if (al0 != 1.f || al1 != 1.f) {
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       st.o[n][0] *= al0;
       st.o[n][1] *= al0;
-      st.o[n][2] *= al1;
-      st.o[n][3] *= al1;
+      if (kHi) {
+        st.o[n][2] *= al1;
+        st.o[n][3] *= al1;
+      }
     }
   }
   uint32_t pa[4];
   pa[0] = DT<T>::from_f2(sc[0][0], sc[0][1]);
-  pa[1] = DT<T>::from_f2(sc[0][2], sc[0][3]);
+  pa[1] = kHi ? DT<T>::from_f2(sc[0][2], sc[0][3]) : 0u;
   pa[2] = DT<T>::from_f2(sc[1][0], sc[1][1]);
-  pa[3] = DT<T>::from_f2(sc[1][2], sc[1][3]);
+  pa[3] = kHi ? DT<T>::from_f2(sc[1][2], sc[1][3]) : 0u;
   // keys this lane's B fragments carry: wtok + cq + {0,1} (b0), + 8 (b1)
   const uint32_t keep_lo = (cq < valid ? 0x0000ffffu : 0u) | (cq + 1 < valid ? 0xffff0000u : 0u);
   const uint32_t keep_hi =

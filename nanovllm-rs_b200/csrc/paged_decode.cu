@@ -47,7 +47,7 @@ struct DecodeParams {
   int* err;
 };
 
-template <typename T>
+template <typename T, bool kHi>
 __global__ void __launch_bounds__(kDecThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
@@ -125,7 +125,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     const uint32_t kbase = smem_u32(smem + s * kDecStageBytes);
     const int valid = tok_end - (tok_begin + it * kDecTile + warp * 16);  // keys of this slice
     if (valid > 0)
-      dec_tile<T>(qa, st, kbase, kbase + kDecTileBytes, warp * 16, valid, p.scale_log2, lane);
+      dec_tile<T, kHi>(qa, st, kbase, kbase + kDecTileBytes, warp * 16, valid, p.scale_log2,
+                       lane);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -300,17 +301,20 @@ int launch_paged_decode(const AttnArgs& a) {
 #else
   dim3 grid(splits, a.hkv, a.num_seqs);
 #endif
+  // group sizes up to 8 leave fragment rows 8..15 as padding (kHi = false)
+  const bool hi = p.group > 8;
   if (a.dtype == NVKV_DTYPE_BF16) {
-    auto kern = paged_decode_kernel<__nv_bfloat16>;
-    static unsigned long long attr_done_1 = 0;
-    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_1);
+    auto kern = hi ? paged_decode_kernel<__nv_bfloat16, true>
+                   : paged_decode_kernel<__nv_bfloat16, false>;
+    static unsigned long long attr_done[2] = {0, 0};
+    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done[hi]);
     if (!rc) rc = launch_pdl(kern, grid, dim3(kDecThreads), kDecSmemBytes, a.stream,
                              "paged decode launch", mk, mv, p);
     if (!rc && splits > 1) rc = launch_combine(decode_combine_kernel<__nv_bfloat16>, p, a);
   } else {
-    auto kern = paged_decode_kernel<__half>;
-    static unsigned long long attr_done_2 = 0;
-    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done_2);
+    auto kern = hi ? paged_decode_kernel<__half, true> : paged_decode_kernel<__half, false>;
+    static unsigned long long attr_done[2] = {0, 0};
+    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done[hi]);
     if (!rc) rc = launch_pdl(kern, grid, dim3(kDecThreads), kDecSmemBytes, a.stream,
                              "paged decode launch", mk, mv, p);
     if (!rc && splits > 1) rc = launch_combine(decode_combine_kernel<__half>, p, a);
