@@ -40,6 +40,7 @@ struct DecodeParams {
   int group;
   int page_size;
   int chunk_tokens;  // keys per split, multiple of kDecTile
+  int max_k;         // max_seqlen_k: the block tables cover this many keys
   int max_splits;
   float scale_log2;
   float* ws_o;    // [B][max_splits][Hq][D]
@@ -81,11 +82,25 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   pdl_launch_dependents();
   pdl_wait();  // inputs may come from the previous kernel in the stream
 
+  // The producer fetches the page of its first tile together with the
+  // sequence lengths (one round trip less before the first TMA).  The index
+  // depends only on the split, and split * chunk_tokens < the plan's key
+  // bound <= page_size * bt_stride (validated on the host), so it is in
+  // bounds even for a split this sequence does not have.
+  uint32_t first_page = 0;
+  if (threadIdx.x == kDecComputeWarps * 32 && p.block_tables)
+    first_page = __ldg(p.block_tables + (int64_t)b * p.bt_stride +
+                       (split * p.chunk_tokens) / p.page_size);
+
   const uint32_t q0 = p.cu_q[b];
   if (p.cu_q[b + 1] - q0 != 1) return;  // not a decode row: the prefill kernel owns it
   const int k_len = (int)(p.cu_k[b + 1] - p.cu_k[b]);
   const int nsplit = k_len > 0 ? (k_len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
   if (split >= nsplit) return;
+  if (k_len > p.max_k) {  // beyond max_seqlen_k the block table may be shorter
+    if (threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
+    return;
+  }
   const int tok_begin = split * p.chunk_tokens;
   const int tok_end = min(k_len, tok_begin + p.chunk_tokens);
   const int ntiles = tok_end > tok_begin ? (tok_end - tok_begin + kDecTile - 1) / kDecTile : 0;
@@ -99,8 +114,19 @@ __global__ void __launch_bounds__(kDecThreads, 2)
         const int s = it % kDecStages;
         const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
         if (it >= kDecStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
-        const int64_t row = dec_tile_row(p.block_tables, p.bt_stride, p.num_blocks, p.page_size,
-                                         p.cu_k, b, tok_begin + it * kDecTile, p.err);
+        const int j0 = tok_begin + it * kDecTile;
+        int64_t row;
+        if (it == 0 && p.block_tables) {
+          uint32_t page = first_page;
+          if ((int64_t)page >= p.num_blocks) {
+            record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
+            page = 0;
+          }
+          row = (int64_t)page * p.page_size + (j0 % p.page_size);
+        } else {
+          row = dec_tile_row(p.block_tables, p.bt_stride, p.num_blocks, p.page_size, p.cu_k, b,
+                             j0, p.err);
+        }
         dec_load_stage(smem + s * kDecStageBytes, &full[s], &tmap_k, &tmap_v, kvh, row);
       }
     }
@@ -286,6 +312,7 @@ int launch_paged_decode(const AttnArgs& a) {
   p.group = a.hq / a.hkv;
   p.page_size = a.page;
   p.chunk_tokens = chunk;
+  p.max_k = a.max_k;
   p.max_splits = splits;
   p.scale_log2 = a.scale * kLog2e;
   p.ws_o = nullptr;

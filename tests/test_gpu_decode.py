@@ -226,3 +226,20 @@ def test_decode_repeated_calls_are_bitwise_identical():
     sub = list(range(0, 256, 16))
     want = _oracle(q[sub], kc, vc, [tables[b] for b in sub], [lens[b] for b in sub])
     assert_attention_close(outs[2][sub], want, "repeat")
+
+
+def test_decode_context_above_max_seqlen_is_reported():
+    """k_len > max_seqlen_k (a caller bug): the block tables only cover
+    max_seqlen_k keys, so the kernel must report DEVERR_SEQLEN rather than
+    read past them; the other sequences are still correct."""
+    g = torch.Generator().manual_seed(31)
+    lens = [500, 200]
+    kc, vc, bt, tables = make_paged(lens, 256, 1, 128, 6, g)
+    q = torch.randn(2, 4, 128, generator=g).to(torch.bfloat16).cuda()
+    bt2 = torch.from_numpy(bt[:, :2].copy().view(np.int32)).cuda()  # 2 pages: 512 keys max
+    nvkv.device_error()
+    out = nvkv.paged_attention(q, kc, vc, cu([1, 1]), cu(lens), bt2, 1, 300, 0.1)
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
+    kb, vb = gather_seq(kc, vc, tables[1], 200)
+    assert_attention_close(out[1:2], O.causal_attention_one(f32(q)[1:2], kb, vb, 0.1), "row 1")
