@@ -253,20 +253,31 @@ __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParam
 // chunks shorter than 12 tiles (768 keys): a sweep over the decode shapes of
 // configs 2, 4 (TP1, TP8) and 5 found this the best or equal-best everywhere
 // (shorter chunks pay per-CTA setup and merge work on small per-GPU batches).
+// Exception: when one CTA per (sequence, kv head) already fills >= 80 % of a
+// resident wave and no sequence exceeds NVKV_DECODE_ONE_WAVE_MAX_TILES tiles,
+// nothing is split -- a single wave with no combine beats 1.7 waves plus a
+// combine (8B TP8, 256 seqs: 37.2 -> 31.1 us at ctx <= 1536, 54.7 -> 45.6 us
+// at ctx <= 2560).  The cost is bounded by the tile cap: one long sequence
+// among short ones then runs unsplit (+1.3 us measured at 24 tiles).
 #ifndef NVKV_DECODE_TARGET_CTAS
 #define NVKV_DECODE_TARGET_CTAS (148 * 2 * 3)
 #endif
 #ifndef NVKV_DECODE_MIN_TILES
 #define NVKV_DECODE_MIN_TILES 12
 #endif
+#ifndef NVKV_DECODE_ONE_WAVE_MAX_TILES
+#define NVKV_DECODE_ONE_WAVE_MAX_TILES 48
+#endif
 void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
                  int* max_splits) {
   const int tiles = max_seqlen_k > 0 ? (max_seqlen_k + kDecTile - 1) / kDecTile : 1;
   const int64_t items = (int64_t)num_seqs * num_kv_heads;
   const int64_t target = NVKV_DECODE_TARGET_CTAS;
+  const int64_t wave = 148 * 2;
   int splits = (int)((target + items - 1) / items);
   const int max_by_len = (tiles + NVKV_DECODE_MIN_TILES - 1) / NVKV_DECODE_MIN_TILES;
   if (splits > max_by_len) splits = max_by_len;
+  if (items * 5 >= wave * 4 && tiles <= NVKV_DECODE_ONE_WAVE_MAX_TILES) splits = 1;
   if (splits < 1) splits = 1;
   const int tiles_per_split = (tiles + splits - 1) / splits;
   *chunk_tokens = tiles_per_split * kDecTile;

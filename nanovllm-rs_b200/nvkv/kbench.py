@@ -164,6 +164,11 @@ CASES = {
         "decode_8b_tp1", np.random.default_rng(4).integers(1025, 1537, 256), 32, 8, 1560, it, 2),
     "decode_8b_tp8": lambda it: case_decode(
         "decode_8b_tp8", np.random.default_rng(4).integers(1025, 1537, 256), 4, 1, 1560, it, 8),
+    "decode_8b_tp8_2k": lambda it: case_decode(
+        "decode_8b_tp8_2k", np.random.default_rng(5).integers(1537, 2561, 256), 4, 1, 2900, it, 8),
+    "decode_8b_tp8_skew": lambda it: case_decode(
+        "decode_8b_tp8_skew", np.concatenate([np.random.default_rng(6).integers(64, 513, 255),
+                                              [1536]]), 4, 1, 600, it, 8),
     "decode_32b_tp8": lambda it: case_decode(
         "decode_32b_tp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
     "prefill_8b": lambda it: case_prefill(it),
