@@ -208,6 +208,29 @@ int nvkv_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, in
                       int64_t num_tokens, int inter, int dtype, nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Device-side metadata of a pure decode step.  Replaces the decode case of
+ * ModelRunner::prepare_model_input (engine/model_runner.rs:69-160) after
+ * Sequence::append (engine/sequence.rs), and the H2D upload of its tensors
+ * (model_runner.rs:134-146), so consecutive decode steps need no host round
+ * trip.  For each of num_seqs sequences (every one decoding one token):
+ *   seq_lens[b] += 1                      (last step's token is appended)
+ *   positions[b] = seq_lens[b] - 1
+ *   slot_mapping[b] = page * page_size + positions[b] % page_size,
+ *     page = block_tables[b * block_table_stride + positions[b] / page_size]
+ *     (-1 and NVKV_DEVERR_BLOCK_RANGE when that entry is past the table or
+ *     page >= num_blocks: the block manager must append the page first)
+ *   cu_seqlens_q[b] = b;  cu_seqlens_k = exclusive-then-total prefix sum of
+ *     seq_lens ([num_seqs + 1]); seq_lens doubles as context_lens.
+ * All buffers are device memory; integer arithmetic, bit-exact with the host.
+ * max_seqlen_k for the attention call stays a host value: pass an upper bound
+ * (e.g. the current maximum plus the number of steps a graph replays).
+ * ---------------------------------------------------------------------- */
+int nvkv_decode_advance(int num_seqs, int page_size, int64_t* seq_lens,
+                        const uint32_t* block_tables, int64_t block_table_stride,
+                        int64_t num_blocks, int64_t* positions, int64_t* slot_mapping,
+                        uint32_t* cu_seqlens_q, uint32_t* cu_seqlens_k, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-parallel epilogue: all-reduce of the row-parallel partial sums,
  * residual add and RMSNorm in ONE kernel over NVLink peer memory.
  *

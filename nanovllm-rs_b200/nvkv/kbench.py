@@ -13,6 +13,7 @@ Cases (one JSON line each; bytes/flops are the algorithmic figures):
   decode_8b_tp8   the same layer at TP8 per GPU (4q/1kv)                   (HBM)
   decode_32b_tp8  Qwen3-32B TP8 per GPU: B=64, 8q/1kv, L=32768            (HBM)
   prefill_8b      tcgen05 prefill, Qwen3-8B TP1: 16 prompts x 1024, causal (tensor)
+  step_metadata   device-side decode-step metadata, 256 sequences (latency)
 Inputs of every HBM case exceed L2 or are rotated through enough copies
 that each timed launch reads cold data.
 """
@@ -136,6 +137,24 @@ def case_decode(name, lens, hq, hkv, nblocks, iters, copies=1):
                 splits=bool(ops.workspace_size(B, hq, hkv, 1, int(max(lens)))), bound="hbm")
 
 
+def case_step_metadata(B, iters, P=256):
+    """nvkv_decode_advance on a B-sequence decode step (lengths U[1025,1536],
+    pages appended ahead): the device replacement of the host-side metadata
+    build + H2D of positions / slot_mapping / cu_seqlens."""
+    rng = np.random.default_rng(7)
+    lens = rng.integers(1025, 1537, B)
+    width = int((lens.max() + 64 * iters + P - 1) // P)
+    bt = torch.from_numpy(rng.permutation(B * width).astype(np.int32).reshape(B, width)).cuda()
+    seq_lens = torch.from_numpy(lens - 1).cuda()
+    pos = torch.empty(B, dtype=torch.int64, device="cuda")
+    slots = torch.empty_like(pos)
+    cuq = torch.empty(B + 1, dtype=torch.int32, device="cuda")
+    cuk = torch.empty_like(cuq)
+    fn = lambda i: ops.decode_advance(seq_lens, bt, B * width, P, pos, slots, cuq, cuk)  # noqa
+    med, _ = _time(fn, iters)
+    return dict(kernel="decode_advance", B=B, bytes=B * (8 * 3 + 4 * 2 + 4), s=med, bound="latency")
+
+
 def case_prefill(iters, nseq=16, L=1024, hq=32, hkv=8):
     page = 256
     lens = [L] * nseq
@@ -172,6 +191,7 @@ CASES = {
     "decode_32b_tp8": lambda it: case_decode(
         "decode_32b_tp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
     "prefill_8b": lambda it: case_prefill(it),
+    "step_metadata": lambda it: case_step_metadata(256, it),
 }
 
 
@@ -183,7 +203,9 @@ def main(argv=None):
     hbm, tf, src = _peaks()
     for name in a.case:
         r = CASES[name](a.iters)
-        if r["bound"] == "hbm":
+        if r["bound"] == "latency":  # a few KB: only the time means anything
+            r.update(case=name, us=round(r["s"] * 1e6, 2))
+        elif r["bound"] == "hbm":
             ach = r["bytes"] / r["s"] / 1e9
             r.update(case=name, us=round(r["s"] * 1e6, 2), achieved_gbs=round(ach, 1),
                      peak_gbs=hbm, frac=round(ach / hbm, 4), peak_source=src)

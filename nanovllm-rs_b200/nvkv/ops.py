@@ -189,3 +189,24 @@ def silu_and_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> t
     check(lib.nvkv_silu_and_mul(_ptr(gate_up), gate_up.stride(0), _ptr(out), out.stride(0), T, F,
                                 _dtype(gate_up), _stream()))
     return out
+
+
+def decode_advance(seq_lens: torch.Tensor, block_tables: torch.Tensor, num_blocks: int,
+                   page_size: int, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                   cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor) -> None:
+    """Device-side metadata of a pure decode step (model_runner.rs:69-160,
+    decode case): seq_lens [B] int64 is advanced by one in place and the
+    step's positions / slot_mapping [B] int64 and cu_seqlens_q/k [B+1]
+    int32 are written, without a host round trip."""
+    B = seq_lens.numel()
+    _need(seq_lens.dtype == torch.int64 and seq_lens.is_cuda and seq_lens.is_contiguous(),
+          "seq_lens: int64 [B] on cuda")
+    _need(block_tables.dim() == 2 and block_tables.size(0) == B and
+          block_tables.dtype == torch.int32 and block_tables.stride(1) == 1, "block_tables")
+    for t, n, dt in ((positions, B, torch.int64), (slot_mapping, B, torch.int64),
+                     (cu_seqlens_q, B + 1, torch.int32), (cu_seqlens_k, B + 1, torch.int32)):
+        _need(t.numel() == n and t.dtype == dt and t.is_contiguous(), "output buffer shape")
+    check(lib.nvkv_decode_advance(B, page_size, _ptr(seq_lens), _ptr(block_tables),
+                                  block_tables.stride(0), int(num_blocks), _ptr(positions),
+                                  _ptr(slot_mapping), _ptr(cu_seqlens_q), _ptr(cu_seqlens_k),
+                                  _stream()))

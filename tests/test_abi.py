@@ -132,3 +132,14 @@ def test_comm_validation_host_only():
                                        None) == ERR_INVALID_ARG
     assert lib.nvkv_comm_set_timeout(None, 1) == ERR_INVALID_ARG
     assert lib.nvkv_comm_destroy(None) == OK
+
+
+def test_decode_advance_validation_host_only():
+    from nvkv._lib import lib, ERR_INVALID_ARG, OK
+    assert lib.nvkv_decode_advance(-1, 256, None, None, 1, 1, None, None, None, None,
+                                   None) == ERR_INVALID_ARG
+    assert lib.nvkv_decode_advance(4, 0, None, None, 1, 1, None, None, None, None,
+                                   None) == ERR_INVALID_ARG
+    assert lib.nvkv_decode_advance(4, 256, None, None, 1, 1, None, None, None, None,
+                                   None) == ERR_INVALID_ARG
+    assert lib.nvkv_decode_advance(0, 256, None, None, 1, 1, None, None, None, None, None) == OK
