@@ -432,6 +432,7 @@ def run_nvkv(a):
             line["collectives"] = ar
         if world == 1:
             line["cpu_baseline"] = cpu_reference(max_seconds=20.0)
+            line["op_level"] = op_level_config2()
         print(json.dumps(line), flush=True)
     # a graph holding NCCL calls must be released before the process group
     run = None
@@ -519,6 +520,122 @@ def _all_host_threads():
     except Exception:
         pass
     return n
+
+
+def op_level_config2(seed=2, reps=20):
+    """BASELINE config 2 at operator level: paged decode attention, B=64 decode
+    queries, 16 q / 8 kv heads, L ~ U[512, 4096], P=256, block tables a seeded
+    permutation of a 2048-block pool, q/k/v ~ N(0,1).  Reports the nvkv kernel
+    (CUDA graph of `reps` calls, CUDA events), the installed flash_attn 2.8.3
+    paged varlen kernel on the same tensors as a labelled reference-class
+    proxy (the FA2 lineage of the reference's candle-flash-attn, run as a
+    black box), and the CPU restatement of the reference path (oracle, numpy
+    fp32, all host threads) on the same batch."""
+    import torch
+
+    from nvkv import ops
+    B, hq, hkv, D, P, pool = 64, 16, 8, 128, 256, 2048
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(512, 4097, B)
+    need = (lens + P - 1) // P
+    perm = rng.permutation(pool).astype(np.int32)
+    bt = np.zeros((B, int(need.max())), np.int32)
+    u = 0
+    for i, n in enumerate(need):
+        bt[i, :n] = perm[u:u + n]
+        u += n
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kc = torch.randn(pool, P, hkv, D, generator=g, device="cuda").bfloat16()
+    vc = torch.randn(pool, P, hkv, D, generator=g, device="cuda").bfloat16()
+    q = torch.randn(B, hq, D, generator=g, device="cuda").bfloat16()
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    cu_k = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).cuda()
+    btd = torch.from_numpy(bt).cuda()
+    max_k, scale = int(lens.max()), D ** -0.5
+    out = torch.empty_like(q)
+    ws = torch.empty(max(16, ops.workspace_size(B, hq, hkv, 1, max_k)), dtype=torch.uint8,
+                     device="cuda")
+
+    def nv():
+        ops.paged_attention(q, kc, vc, cu_q, cu_k, btd, 1, max_k, scale, out=out, workspace=ws)
+
+    def graph_us(fn):
+        fn()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for _ in range(reps):
+                fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        gr.reset()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    nbytes = int(lens.sum()) * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * int(need.sum())
+    nv_us = graph_us(nv)
+    peak, _ = load_peak()
+    res = {"workload": "BASELINE config 2: paged decode attention, B=64, 16q/8kv, D=128, "
+                       "L~U[512,4096], P=256, 2048-block pool, bf16",
+           "nvkv_us": round(nv_us, 2),
+           "nvkv_gbs": round(nbytes / (nv_us * 1e-6) / 1e9, 1),
+           "nvkv_frac_of_measured_hbm": round(nbytes / (nv_us * 1e-6) / 1e9 / peak, 4),
+           "bytes": nbytes}
+    try:
+        from flash_attn import flash_attn_varlen_func
+        fa_out = {}
+
+        def fa():
+            fa_out["o"] = flash_attn_varlen_func(q, kc, vc, cu_q, cu_k, 1, max_k,
+                                                 softmax_scale=scale, causal=True,
+                                                 block_table=btd)
+
+        fa_us = graph_us(fa)
+        fa()
+        torch.cuda.synchronize()
+        res["flash_attn_proxy"] = {
+            "us": round(fa_us, 2), "gbs": round(nbytes / (fa_us * 1e-6) / 1e9, 1),
+            "nvkv_speedup": round(fa_us / nv_us, 3),
+            "max_abs_diff_vs_nvkv": round(float((fa_out["o"].float() - out.float()).abs().max()),
+                                          5),
+            "label": "flash_attn 2.8.3 flash_attn_varlen_func(block_table=...), black box"}
+    except Exception as ex:  # not part of the product path: a proxy only
+        res["flash_attn_proxy"] = {"unavailable": repr(ex)[:200]}
+    # CPU restatement of the reference path on the same batch (rank 0, host cores)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import nvkv_oracle as O
+    cores = _all_host_threads()
+    qn = q.float().cpu().numpy()
+    seqs = []
+    for b in range(B):  # the paged gather (layers/attention.rs:143-164), done once
+        pages = torch.from_numpy(bt[b, :need[b]].astype(np.int64)).cuda()
+        kb = kc.index_select(0, pages).reshape(-1, hkv, D)[:lens[b]].float().cpu().numpy()
+        vb = vc.index_select(0, pages).reshape(-1, hkv, D)[:lens[b]].float().cpu().numpy()
+        seqs.append((kb, vb))
+    t0 = time.perf_counter()
+    n_done = 0
+    while True:
+        for b in range(B):
+            O.causal_attention_one(qn[b:b + 1], seqs[b][0], seqs[b][1], scale, acc=np.float32)
+        n_done += 1
+        if time.perf_counter() - t0 > 5.0 or n_done >= 3:
+            break
+    cpu_us = (time.perf_counter() - t0) / n_done * 1e6
+    res["cpu_baseline"] = {"us": round(cpu_us, 1), "cores": cores, "kind": "port",
+                           "nvkv_speedup": round(cpu_us / nv_us, 1),
+                           "sample": "the whole config-2 batch: oracle causal_attention_one per "
+                                     "sequence (numpy fp32, unfused softmax attention), the "
+                                     "paged gather done beforehand"}
+    return res
 
 
 def cpu_reference(max_seconds=20.0, reps=None, warmup=1, num_tokens=32, layers=2, vocab_frac=32):

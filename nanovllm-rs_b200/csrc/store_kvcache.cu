@@ -23,6 +23,13 @@ struct VecT<4> { using type = uint32_t; };
 template <>
 struct VecT<2> { using type = uint16_t; };
 
+// A block walks kStoreTok tokens at a time; thread i moves chunks i, i + 256,
+// ... of the token's K row then V row (2 * chunks_per_row per token, no
+// division).  The row loads do not depend on the slot (the source row always
+// exists), so all kStoreTok loads and their slots are in flight together
+// before the slot checks decide which stores happen.
+constexpr int kStoreTok = 4;
+
 template <int VEC>
 __global__ void __launch_bounds__(256) store_kvcache_kernel(
     const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
@@ -31,24 +38,37 @@ __global__ void __launch_bounds__(256) store_kvcache_kernel(
     int64_t key_stride_b, int64_t value_stride_b, int64_t row_bytes, int64_t num_slots,
     int* err) {
   using V = typename VecT<VEC>::type;
-  const int64_t per_tok = 2 * chunks_per_row;
-  const int64_t total = num_tokens * per_tok;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = idx / per_tok;
-    const int64_t r = idx - t * per_tok;
-    const bool is_v = r >= chunks_per_row;
-    const int64_t c = is_v ? r - chunks_per_row : r;
-    const int64_t slot = __ldg(slot_mapping + t);
-    if (slot < 0) continue;  // padded / warm-up token
-    if (slot >= num_slots) {
-      record_error(err, NVKV_DEVERR_SLOT_RANGE);
-      continue;
+  const int per_tok = (int)(2 * chunks_per_row);
+  for (int64_t t0 = (int64_t)blockIdx.x * kStoreTok; t0 < num_tokens;
+       t0 += (int64_t)gridDim.x * kStoreTok) {
+    for (int r = threadIdx.x; r < per_tok; r += blockDim.x) {
+      const bool is_v = r >= chunks_per_row;
+      const int c = is_v ? r - (int)chunks_per_row : r;
+      const uint8_t* base = is_v ? value : key;
+      const int64_t stride = is_v ? value_stride_b : key_stride_b;
+      uint8_t* cache = is_v ? v_cache : k_cache;
+      V x[kStoreTok];
+      int64_t slot[kStoreTok];
+#pragma unroll
+      for (int u = 0; u < kStoreTok; ++u) {
+        const int64_t t = t0 + u;
+        if (t < num_tokens) {
+          slot[u] = __ldg(slot_mapping + t);
+          x[u] = __ldg(reinterpret_cast<const V*>(base + t * stride) + c);
+        } else {
+          slot[u] = -1;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kStoreTok; ++u) {
+        if (slot[u] < 0) continue;  // padded / warm-up token (or past the batch)
+        if (slot[u] >= num_slots) {
+          record_error(err, NVKV_DEVERR_SLOT_RANGE);
+          continue;
+        }
+        reinterpret_cast<V*>(cache + slot[u] * row_bytes)[c] = x[u];
+      }
     }
-    const uint8_t* src = is_v ? value + t * value_stride_b : key + t * key_stride_b;
-    uint8_t* dst = (is_v ? v_cache : k_cache) + slot * row_bytes;
-    V x = __ldg(reinterpret_cast<const V*>(src) + c);
-    reinterpret_cast<V*>(dst)[c] = x;
   }
 }
 
@@ -65,9 +85,10 @@ int launch_store_kvcache(const void* key, const void* value, void* k_cache, void
   };
   const int vec = fits(16) ? 16 : fits(8) ? 8 : fits(4) ? 4 : 2;
   const int64_t cpr = row_bytes / vec;
-  const int64_t total = num_tokens * 2 * cpr;
-  int64_t blocks = (total + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (2 * cpr > 0x7fffffffLL)
+    return set_error(NVKV_ERR_UNSUPPORTED, "store_kvcache: row too wide");
+  int64_t blocks = (num_tokens + kStoreTok - 1) / kStoreTok;
+  if (blocks > 148 * 8) blocks = 148 * 8;  // 8 resident blocks of 256 threads per SM
   int* err = device_error_word();
   auto k = reinterpret_cast<const uint8_t*>(key);
   auto v = reinterpret_cast<const uint8_t*>(value);
