@@ -143,3 +143,24 @@ def test_decode_advance_validation_host_only():
     assert lib.nvkv_decode_advance(4, 256, None, None, 1, 1, None, None, None, None,
                                    None) == ERR_INVALID_ARG
     assert lib.nvkv_decode_advance(0, 256, None, None, 1, 1, None, None, None, None, None) == OK
+
+
+def test_decode_plan_one_wave_rule():
+    """The split-KV plan, seen through the workspace query: a batch whose
+    (sequence, kv head) items fill >= 80 % of a 296-CTA wave with contexts of
+    at most 48 tiles (3072 keys) is not split (no workspace); longer contexts
+    or fewer items keep splitting."""
+    from nvkv._lib import lib
+    need = ctypes.c_size_t(0)
+
+    def ws(B, hq, hkv, max_k):
+        assert lib.nvkv_paged_attention_workspace_size(B, hq, hkv, 128, 1, max_k,
+                                                       ctypes.byref(need)) == 0
+        return need.value
+    assert ws(256, 4, 1, 1536) == 0      # 8B TP8 decode: 256 items, 24 tiles
+    assert ws(256, 4, 1, 3072) == 0      # 48 tiles: still one wave
+    assert ws(256, 4, 1, 3073) > 0       # 49 tiles: split
+    assert ws(237, 4, 1, 1536) == 0      # 237 items >= 0.8 * 296
+    assert ws(236, 4, 1, 1536) > 0       # below: split to fill the machine
+    assert ws(64, 16, 8, 4096) > 0       # config 2: 64-tile contexts split
+    assert ws(64, 8, 1, 32768) > 0       # 32B TP8 long context
