@@ -193,6 +193,50 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
+// Packed two-lane f32 arithmetic (PTX add/sub/fma .f32x2, sm_100): one
+// instruction for two values on the FMA pipe.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// ex2_poly on two values: the same operations in the same order per lane,
+// with the f32 adds and FMAs issued as packed pairs.
+__device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = f2_add(x, magic);
+  const float2 tv = f2_unpack(t);
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));
+  uint64_t p = f2_fma(f2_pack(0.05517153f, 0.05517153f), f, f2_pack(0.24261111f, 0.24261111f));
+  p = f2_fma(p, f, f2_pack(0.69326103f, 0.69326103f));
+  p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+  const float2 pv = f2_unpack(p);
+  const int n0 = __float_as_int(tv.x) - 0x4B400000, n1 = __float_as_int(tv.y) - 0x4B400000;
+  return make_float2(__int_as_float(__float_as_int(pv.x) + (n0 << 23)),
+                     __int_as_float(__float_as_int(pv.y) + (n1 << 23)));
+}
+
 // Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bit.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
@@ -228,7 +272,8 @@ template <typename T, bool kMask>
 __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim, float scale_log2,
                                              float m_use, uint8_t* half, uint32_t row,
                                              float& mx) {
-  float rs = 0.f;
+  uint64_t rs2 = f2_pack(0.f, 0.f);  // the row sum in two packed lanes
+  const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_use, -m_use);
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     uint32_t pk[4];
@@ -241,20 +286,29 @@ __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim
         s1 = kbase + i + 1 <= lim ? s1 : -INFINITY;
       }
       mx = fmaxf(mx, fmaxf(s0, s1));
-      const float x0 = fmaf(s0, scale_log2, -m_use), x1 = fmaf(s1, scale_log2, -m_use);
-      float e0 = (e == 0) ? ex2_mufu(x0) : ex2_poly(x0);
-      float e1 = ex2_poly(x1);
+      const float2 xx = f2_unpack(f2_fma(f2_pack(s0, s1), sc2, nm2));
+      const float x0 = xx.x, x1 = xx.y;
+      float e0, e1;
+      if (e == 0) {  // one exponential in eight on MUFU, the rest on the FMA pipe
+        e0 = ex2_mufu(x0);
+        e1 = ex2_poly(x1);
+      } else {
+        const float2 ee = ex2_poly2(x0, x1);
+        e0 = ee.x;
+        e1 = ee.y;
+      }
       if (kMask) {
         e0 = kbase + i <= lim ? e0 : 0.f;
         e1 = kbase + i + 1 <= lim ? e1 : 0.f;
       }
-      rs += e0 + e1;
+      rs2 = f2_add(rs2, f2_pack(e0, e1));
       pk[e >> 1] = pack_p<T>(e0, e1);
     }
     *reinterpret_cast<uint4*>(half + sw128_offset(row, (uint32_t)u)) =
         make_uint4(pk[0], pk[1], pk[2], pk[3]);
   }
-  return rs;
+  const float2 rs = f2_unpack(rs2);
+  return rs.x + rs.y;
 }
 
 // S_x = Q_x . K^T over D = 128: 8 MMAs of K = 16, advancing 32 bytes inside
