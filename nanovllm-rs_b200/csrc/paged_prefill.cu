@@ -26,8 +26,11 @@
 //               when the max grew by more than 2^8 -- otherwise it keeps the
 //               stale max, whose exponentials stay <= 256 and exact enough in
 //               fp32/bf16 -- then writes P = 2^(s*scale - m) into a swizzled
-//               K-major shared-memory tile.  Half of the exponentials use the
-//               MUFU ex2 unit, half a degree-3 polynomial on the FMA pipe.
+//               K-major shared-memory tile.  The exponentials run on the
+//               MUFU ex2 unit; the scaling FMAs and the row sum use packed
+//               f32x2 instructions (the FMA pipe, not MUFU, is the busier
+//               one here: moving exponentials from a polynomial on the FMA
+//               pipe to MUFU measured 308 -> 272 us on the 8B prefill).
 //   O accumulates in TMEM across key tiles (PV MMAs chain with
 //   accumulate = 1); the epilogue divides by the row sum and stores bf16/f16.
 // Roofline: tensor cores; flops = 4 * D * (visible (query, key) pairs).
@@ -177,23 +180,15 @@ __device__ __forceinline__ float ex2_mufu(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2];
-// 2^f by a degree-3 polynomial fitted here to the exact function (max
-// relative error 7.5e-5, far below bf16's 2^-9 half-ulp); 2^n is added into
-// the exponent bits.  Valid for x in [-125, 126]; smaller x is clamped (the
-// result, ~2^-125, is negligible next to the row sum it joins).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;  // 1.5 * 2^23: t's low mantissa bits hold round(x)
-  const int n = __float_as_int(t) - 0x4B400000;
-  const float f = x - (t - 12582912.0f);
-  float p = fmaf(0.05517153f, f, 0.24261111f);
-  p = fmaf(p, f, 0.69326103f);
-  p = fmaf(p, f, 0.99992806f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
+// max(a, b, c) in one instruction (three-input PTX max.f32; NaN handling as
+// fmaxf: a NaN operand is ignored).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
-// Packed two-lane f32 arithmetic (PTX add/sub/fma .f32x2, sm_100): one
+// Packed two-lane f32 arithmetic (PTX add/fma .f32x2, sm_100): one
 // instruction for two values on the FMA pipe.
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
   uint64_t r;
@@ -215,28 +210,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-// ex2_poly on two values: the same operations in the same order per lane,
-// with the f32 adds and FMAs issued as packed pairs.
-__device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
-  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const uint64_t t = f2_add(x, magic);
-  const float2 tv = f2_unpack(t);
-  const uint64_t f = f2_sub(x, f2_sub(t, magic));
-  uint64_t p = f2_fma(f2_pack(0.05517153f, 0.05517153f), f, f2_pack(0.24261111f, 0.24261111f));
-  p = f2_fma(p, f, f2_pack(0.69326103f, 0.69326103f));
-  p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
-  const float2 pv = f2_unpack(p);
-  const int n0 = __float_as_int(tv.x) - 0x4B400000, n1 = __float_as_int(tv.y) - 0x4B400000;
-  return make_float2(__int_as_float(__float_as_int(pv.x) + (n0 << 23)),
-                     __int_as_float(__float_as_int(pv.y) + (n1 << 23)));
-}
-
 // Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bit.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
@@ -248,26 +221,17 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, uint32_t b_mn
          ((uint32_t)(kPfBN >> 3) << 17) | ((uint32_t)(kPfBM >> 4) << 24);
 }
 
-// Two P values -> one packed 16-bit pair.  bf16: round-half-up on the integer
-// bits and a byte permute (ALU pipe) instead of a conversion instruction (XU
-// pipe, the softmax bottleneck); P >= 0 and finite, and exact ties (the only
-// inputs where this differs from round-to-nearest-even) occur with
-// probability 2^-16.  f16 keeps the conversion instruction.
+// Two P values -> one packed 16-bit pair (cvt.rn.*x2.f32, round to nearest
+// even).  A byte-permute packing on the ALU was measured slower (271 vs
+// 264 us on the 8B prefill) once the exponentials moved to MUFU.
 template <typename T>
-__device__ __forceinline__ uint32_t pack_p(float a, float b);
-template <>
-__device__ __forceinline__ uint32_t pack_p<__nv_bfloat16>(float a, float b) {
-  return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
-}
-template <>
-__device__ __forceinline__ uint32_t pack_p<__half>(float a, float b) {
-  return DT<__half>::from_f2(a, b);
+__device__ __forceinline__ uint32_t pack_p(float a, float b) {
+  return DT<T>::from_f2(a, b);
 }
 
-// P for one 64-key half of a row: e = 2^(s*scale - m) (masked keys -> 0),
-// a quarter on the MUFU unit and the rest on the FMA pipe, packed into the
-// swizzled K-major tile; returns the sum of the e values and folds the
-// half's max of s into `mx`.
+// P for one 64-key half of a row: e = 2^(s*scale - m) (masked keys -> 0) on
+// the MUFU unit, packed into the swizzled K-major tile; returns the sum of
+// the e values and folds the half's max of s into `mx`.
 template <typename T, bool kMask>
 __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim, float scale_log2,
                                              float m_use, uint8_t* half, uint32_t row,
@@ -285,18 +249,10 @@ __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim
         s0 = kbase + i <= lim ? s0 : -INFINITY;
         s1 = kbase + i + 1 <= lim ? s1 : -INFINITY;
       }
-      mx = fmaxf(mx, fmaxf(s0, s1));
+      mx = fmax3(mx, s0, s1);
       const float2 xx = f2_unpack(f2_fma(f2_pack(s0, s1), sc2, nm2));
       const float x0 = xx.x, x1 = xx.y;
-      float e0, e1;
-      if (e == 0) {  // one exponential in eight on MUFU, the rest on the FMA pipe
-        e0 = ex2_mufu(x0);
-        e1 = ex2_poly(x1);
-      } else {
-        const float2 ee = ex2_poly2(x0, x1);
-        e0 = ee.x;
-        e1 = ee.y;
-      }
+      float e0 = ex2_mufu(x0), e1 = ex2_mufu(x1);
       if (kMask) {
         e0 = kbase + i <= lim ? e0 : 0.f;
         e1 = kbase + i + 1 <= lim ? e1 : 0.f;
@@ -554,7 +510,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 64; ++i) mx = fmaxf(mx, h * 64 + i <= lim ? sv[i] : -INFINITY);
+            for (int i = 0; i < 64; i += 2)
+              mx = fmax3(mx, h * 64 + i <= lim ? sv[i] : -INFINITY,
+                         h * 64 + i + 1 <= lim ? sv[i + 1] : -INFINITY);
           }
           const float m_new = fmaxf(m_ref, mx * p.scale_log2);
           const bool need = m_new > m_ref + kPfRescaleLog2;
