@@ -34,6 +34,7 @@
 //   O accumulates in TMEM across key tiles (PV MMAs chain with
 //   accumulate = 1); the epilogue divides by the row sum and stores bf16/f16.
 // Roofline: tensor cores; flops = 4 * D * (visible (query, key) pairs).
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -53,9 +54,10 @@ constexpr int kPfOffKV = kPfOffQB + kPfTile;
 constexpr int kPfOffPA = kPfOffKV + kPfSlots * kPfTile;
 constexpr int kPfOffPB = kPfOffPA + kPfTile;
 constexpr int kPfOffBar = kPfOffPB + kPfTile;
-constexpr int kPfNumBars = 1 + 2 * kPfSlots + 8;
+constexpr int kPfNumBars = 2 + 2 * kPfSlots + 8;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
+constexpr int kPfCtas = 148;  // B200 SMs
 constexpr float kPfRescaleLog2 = 8.0f;  // rescale O only when the max grows by > 2^8
 
 static_assert(kPfSmemBytes <= 232448, "prefill shared memory exceeds 227 KB");
@@ -72,6 +74,9 @@ struct PrefillParams {
   int pair;  // 1: slots A/B are heads 2p, 2p+1 of one kv group; 0: slot A only
   int page_size;
   int num_q_tiles;
+  int num_head_slots;  // CTAs' head dimension: hq / 2 with pairs, else hq
+  int num_seqs;
+  int num_items;       // num_q_tiles * num_head_slots * num_seqs
   int causal;
   float scale_log2;
   int* err;
@@ -289,6 +294,45 @@ __device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t sp, uint32
   }
 }
 
+// One work item = (q tile, head pair / head, sequence).  Items are numbered
+// q-tile-major with the heaviest causal tiles (last q tile) first, then head
+// slot, then sequence; CTA c takes items c, c + gridDim.x, ...  Returns 1 for
+// an item with work, 0 for an empty one (q_len <= 1: decode rows, or a tile
+// past q_len), -1 for a sequence with k_len < q_len (an error).
+struct PfItem {
+  int b, head0, kvh, i0, q_len, k_len, off, ntiles;
+  uint32_t qs, ks;
+};
+__device__ __forceinline__ int pf_item(const PrefillParams& p, int w, PfItem& it) {
+  const int per_tile = p.num_head_slots * p.num_seqs;
+  const int qt = p.num_q_tiles - 1 - w / per_tile;
+  const int rem = w % per_tile;
+  const int y = rem % p.num_head_slots;
+  it.b = rem / p.num_head_slots;
+  it.head0 = p.pair ? 2 * y : y;
+  it.kvh = it.head0 / p.group;
+  it.qs = __ldg(p.cu_q + it.b);
+  it.q_len = (int)(__ldg(p.cu_q + it.b + 1) - it.qs);
+  it.i0 = qt * kPfBM;
+  if (it.q_len <= 1 || it.i0 >= it.q_len) return 0;  // q_len == 1 rows: decode kernel
+  it.ks = __ldg(p.cu_k + it.b);
+  it.k_len = (int)(__ldg(p.cu_k + it.b + 1) - it.ks);
+  it.off = it.k_len - it.q_len;
+  if (it.off < 0) return -1;
+  const int last_row = min(it.i0 + kPfBM, it.q_len) - 1;
+  const int kmax = p.causal ? min(it.k_len, last_row + it.off + 1) : it.k_len;
+  it.ntiles = (kmax + kPfBN - 1) / kPfBN;
+  return 1;
+}
+
+// Persistent: one CTA per SM walks its items with the barriers, TMEM and
+// descriptors set up once.  Every barrier phase is a running count over the
+// CTA's items (g = key tiles so far per slot, t = K/V ring loads, nq =
+// items), so the MMA warp issues item i+1's first S while the softmax warps
+// still run item i's epilogue, and the producer loads item i+1's Q as soon as
+// item i's last S MMA has read Q (q_empty).  O_x needs no extra barrier: its
+// next overwrite (item i+1's first PV, accumulate = 0) waits on p_full, which
+// the softmax warps arrive only after their epilogue has read O_x.
 template <typename T>
 __global__ void __launch_bounds__(kPfThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -299,39 +343,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPfOffBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;             // [kPfSlots]
+  uint64_t* q_empty = bars + 1;             // the item's last S MMA has read Q
+  uint64_t* kv_full = bars + 2;             // [kPfSlots]
   uint64_t* kv_empty = kv_full + kPfSlots;  // [kPfSlots]
   uint64_t* s_full = kv_empty + kPfSlots;   // [2]: S_x written by the MMA
   uint64_t* s_free = s_full + 2;            // [2]: S_x read by its softmax warpgroup
-  uint64_t* p_full = s_free + 2;            // [2]: P_x written (and O_x rescaled)
+  uint64_t* p_full = s_free + 2;            // [2]: P_x written (and O_x rescaled / read)
   uint64_t* o_done = p_full + 2;            // [2]: PV_x finished (O_x stable, P_x free)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
-  const int qt = p.num_q_tiles - 1 - (int)blockIdx.x;  // heaviest causal tiles first
-  const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nslot = p.pair ? 2 : 1;
-  const int head0 = p.pair ? 2 * (int)blockIdx.y : (int)blockIdx.y;
-  const int kvh = head0 / p.group;
-
-  const uint32_t qs = p.cu_q[b];
-  const int q_len = (int)(p.cu_q[b + 1] - qs);
-  if (q_len <= 1) return;  // q_len == 1 rows belong to the decode kernel
-  const int i0 = qt * kPfBM;
-  if (i0 >= q_len) return;
-  const uint32_t ks = p.cu_k[b];
-  const int k_len = (int)(p.cu_k[b + 1] - ks);
-  const int off = k_len - q_len;
-  if (off < 0) {
-    if (threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
-    return;
-  }
-  const int last_row = min(i0 + kPfBM, q_len) - 1;
-  const int kmax = p.causal ? min(k_len, last_row + off + 1) : k_len;
-  const int ntiles = (kmax + kPfBN - 1) / kPfBN;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < kPfSlots; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -359,34 +385,47 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
-      mbar_arrive_expect_tx(q_full, nslot * kPfTile);
-      for (int x = 0; x < nslot; ++x) {
-        uint8_t* qd = smem + (x ? kPfOffQB : kPfOffQA);
-        tma_load_3d(qd, &tmap_q, q_full, 0, head0 + x, (int)(qs + i0));
-        tma_load_3d(qd + kPfHalf, &tmap_q, q_full, 64, head0 + x, (int)(qs + i0));
-      }
-      for (int t = 0; t < 2 * ntiles; ++t) {  // K_0, V_0, K_1, V_1, ...
-        const int j = t >> 1;
-        const int s = t % kPfSlots;
-        const uint32_t ph = (uint32_t)(t / kPfSlots) & 1u;
-        if (t >= kPfSlots && !mbar_wait(&kv_empty[s], ph ^ 1u, p.err)) break;
-        const int j0 = j * kPfBN;
-        int64_t row;
-        if (p.block_tables) {
-          uint32_t page = p.block_tables[(int64_t)b * p.bt_stride + j0 / p.page_size];
-          if ((int64_t)page >= p.num_blocks) {
-            record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
-            page = 0;
-          }
-          row = (int64_t)page * p.page_size + (j0 % p.page_size);
-        } else {
-          row = (int64_t)ks + j0;
+      uint32_t nq = 0, t = 0;  // items loaded, K/V ring loads (running over items)
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < p.num_items; w += gridDim.x) {
+        PfItem it;
+        const int kind = pf_item(p, w, it);
+        if (kind < 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
+        if (kind <= 0) continue;
+        if (nq > 0 && !mbar_wait(q_empty, (nq - 1) & 1u, p.err)) break;
+        mbar_arrive_expect_tx(q_full, nslot * kPfTile);
+        for (int x = 0; x < nslot; ++x) {
+          uint8_t* qd = smem + (x ? kPfOffQB : kPfOffQA);
+          tma_load_3d(qd, &tmap_q, q_full, 0, it.head0 + x, (int)(it.qs + it.i0));
+          tma_load_3d(qd + kPfHalf, &tmap_q, q_full, 64, it.head0 + x, (int)(it.qs + it.i0));
         }
-        uint8_t* dst = smem + kPfOffKV + s * kPfTile;
-        const CUtensorMap* map = (t & 1) ? &tmap_v : &tmap_k;
-        mbar_arrive_expect_tx(&kv_full[s], kPfTile);
-        tma_load_3d(dst, map, &kv_full[s], 0, kvh, (int)row);
-        tma_load_3d(dst + kPfHalf, map, &kv_full[s], 64, kvh, (int)row);
+        ++nq;
+        for (int u = 0; u < 2 * it.ntiles; ++u, ++t) {  // K_0, V_0, K_1, V_1, ...
+          const int j = u >> 1;
+          const int s = (int)(t % kPfSlots);
+          const uint32_t ph = (t / kPfSlots) & 1u;
+          if (t >= kPfSlots && !mbar_wait(&kv_empty[s], ph ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          const int j0 = j * kPfBN;
+          int64_t row;
+          if (p.block_tables) {
+            uint32_t page = p.block_tables[(int64_t)it.b * p.bt_stride + j0 / p.page_size];
+            if ((int64_t)page >= p.num_blocks) {
+              record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
+              page = 0;
+            }
+            row = (int64_t)page * p.page_size + (j0 % p.page_size);
+          } else {
+            row = (int64_t)it.ks + j0;
+          }
+          uint8_t* dst = smem + kPfOffKV + s * kPfTile;
+          const CUtensorMap* map = (u & 1) ? &tmap_v : &tmap_k;
+          mbar_arrive_expect_tx(&kv_full[s], kPfTile);
+          tma_load_3d(dst, map, &kv_full[s], 0, it.kvh, (int)row);
+          tma_load_3d(dst + kPfHalf, map, &kv_full[s], 64, it.kvh, (int)row);
+        }
       }
     }
   } else if (warp == 1) {
@@ -401,49 +440,66 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #define PF_SLOT(t) (kv0 + (uint32_t)((t) % kPfSlots) * kPfTile)
 #define PF_PAR(t) ((uint32_t)((t) / kPfSlots) & 1u)
 #define PF_FULL(t) (&kv_full[(t) % kPfSlots])
-      bool ok = mbar_wait(q_full, 0, p.err) && mbar_wait(PF_FULL(0), PF_PAR(0), p.err);
-      if (ok) {
-        tc_fence_after();
-        pf_issue_s(tmem + 0u, sqa, PF_SLOT(0), idesc_qk);
-        tc_commit(&s_full[0]);
-        if (p.pair) {
-          pf_issue_s(tmem + 128u, sqb, PF_SLOT(0), idesc_qk);
-          tc_commit(&s_full[1]);
-        }
-        tc_commit(&kv_empty[0]);
-      }
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const uint32_t pj = (uint32_t)j & 1u;
-        const bool more = j + 1 < ntiles;
-        const int tv = 2 * j + 1, tk = 2 * j + 2;  // V_j and K_{j+1} in the load order
-        ok = mbar_wait(PF_FULL(tv), PF_PAR(tv), p.err) && mbar_wait(&p_full[0], pj, p.err);
+      uint32_t nq = 0, t = 0, g = 0;  // items, K/V ring position, key tiles per slot
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < p.num_items; w += gridDim.x) {
+        PfItem it;
+        if (pf_item(p, w, it) <= 0) continue;
+        const int n = it.ntiles;
+        // S_x(g) of the item's first key tile: Q, K_0, and S_x(g - 1) read
+        ok = mbar_wait(q_full, nq & 1u, p.err) && mbar_wait(PF_FULL(t), PF_PAR(t), p.err) &&
+             (g == 0 || mbar_wait(&s_free[0], (g - 1) & 1u, p.err));
         if (!ok) break;
         tc_fence_after();
-        pf_issue_pv(tmem + 256u, spa, PF_SLOT(tv), idesc_pv, j > 0);
-        tc_commit(&o_done[0]);
-        if (more) {
-          ok = mbar_wait(PF_FULL(tk), PF_PAR(tk), p.err) && mbar_wait(&s_free[0], pj, p.err);
+        pf_issue_s(tmem + 0u, sqa, PF_SLOT(t), idesc_qk);
+        tc_commit(&s_full[0]);
+        if (p.pair) {
+          ok = g == 0 || mbar_wait(&s_free[1], (g - 1) & 1u, p.err);
           if (!ok) break;
           tc_fence_after();
-          pf_issue_s(tmem + 0u, sqa, PF_SLOT(tk), idesc_qk);
-          tc_commit(&s_full[0]);
+          pf_issue_s(tmem + 128u, sqb, PF_SLOT(t), idesc_qk);
+          tc_commit(&s_full[1]);
         }
-        if (p.pair) {
-          if (!mbar_wait(&p_full[1], pj, p.err)) break;
+        tc_commit(&kv_empty[t % kPfSlots]);
+        if (n == 1) tc_commit(q_empty);
+        ++nq;
+        for (int j = 0; j < n; ++j, ++g) {
+          const uint32_t pj = g & 1u;
+          const bool more = j + 1 < n;
+          const uint32_t tv = t + 2 * j + 1, tk = t + 2 * j + 2;  // V_j, K_{j+1}
+          ok = mbar_wait(PF_FULL(tv), PF_PAR(tv), p.err) && mbar_wait(&p_full[0], pj, p.err);
+          if (!ok) break;
           tc_fence_after();
-          pf_issue_pv(tmem + 384u, spb, PF_SLOT(tv), idesc_pv, j > 0);
-          tc_commit(&o_done[1]);
-        }
-        tc_commit(&kv_empty[tv % kPfSlots]);  // V_j: both P.V issued
-        if (more) {
-          if (p.pair) {
-            if (!mbar_wait(&s_free[1], pj, p.err)) break;
+          pf_issue_pv(tmem + 256u, spa, PF_SLOT(tv), idesc_pv, j > 0);
+          tc_commit(&o_done[0]);
+          if (more) {
+            ok = mbar_wait(PF_FULL(tk), PF_PAR(tk), p.err) && mbar_wait(&s_free[0], pj, p.err);
+            if (!ok) break;
             tc_fence_after();
-            pf_issue_s(tmem + 128u, sqb, PF_SLOT(tk), idesc_qk);
-            tc_commit(&s_full[1]);
+            pf_issue_s(tmem + 0u, sqa, PF_SLOT(tk), idesc_qk);
+            tc_commit(&s_full[0]);
           }
-          tc_commit(&kv_empty[tk % kPfSlots]);  // K_{j+1}: both S issued
+          if (p.pair) {
+            ok = mbar_wait(&p_full[1], pj, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            pf_issue_pv(tmem + 384u, spb, PF_SLOT(tv), idesc_pv, j > 0);
+            tc_commit(&o_done[1]);
+          }
+          tc_commit(&kv_empty[tv % kPfSlots]);  // V_j: both P.V issued
+          if (more) {
+            if (p.pair) {
+              ok = mbar_wait(&s_free[1], pj, p.err);
+              if (!ok) break;
+              tc_fence_after();
+              pf_issue_s(tmem + 128u, sqb, PF_SLOT(tk), idesc_qk);
+              tc_commit(&s_full[1]);
+            }
+            tc_commit(&kv_empty[tk % kPfSlots]);  // K_{j+1}: both S issued
+            if (j + 2 == n) tc_commit(q_empty);   // the item's last S MMAs read Q
+          }
         }
+        t += 2 * (uint32_t)n;
       }
 #undef PF_SLOT
 #undef PF_PAR
@@ -457,124 +513,136 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int r = quarter * 32 + lane;
       const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
       const uint32_t col_s = x ? 128u : 0u, col_o = x ? 384u : 256u;
-      const int qi = i0 + r;
-      const int lim_row = p.causal ? min(k_len - 1, qi + off) : k_len - 1;
       uint8_t* ptile = smem + (x ? kPfOffPB : kPfOffPA);
-      float m_ref = -INFINITY, l = 0.f;
+      uint32_t g = 0;  // key tiles of this slot so far (running over items)
       bool alive = true;
-      for (int j = 0; j < ntiles; ++j) {
-        const uint32_t pj = (uint32_t)j & 1u;
-        // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], pj, p.err))) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        const int lim = lim_row - j * kPfBN;  // keys c <= lim are visible
-        // the whole warp sees every key of this tile: no masking needed
-        const bool vis = __all_sync(0xffffffffu, lim >= kPfBN - 1);
-        if (j >= 1) {  // PV_x(j-1) done: O_x is stable and the P_x tile is free
-          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[x], pj ^ 1u, p.err))) {
+      for (int w = blockIdx.x; alive && w < p.num_items; w += gridDim.x) {
+        PfItem it;
+        if (pf_item(p, w, it) <= 0) continue;
+        const int qi = it.i0 + r;
+        const int lim_row = p.causal ? min(it.k_len - 1, qi + it.off) : it.k_len - 1;
+        float m_ref = -INFINITY, l = 0.f;
+        for (int j = 0; j < it.ntiles; ++j, ++g) {
+          const uint32_t pj = g & 1u;
+          // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned
+          if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], pj, p.err))) {
             alive = false;
             break;
           }
           tc_fence_after();
-        }
-        float rs = 0.f, mx = -INFINITY;
-        bool redo = (j == 0);
-        if (!redo) {
-          // one pass with the current reference max m_ref (exponentials <= 2^8
-          // unless the row max jumped, which the check below catches)
-          const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            float sv[64];
-            tmem_ld32(lane_addr + col_s + h * 64, sv);
-            tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
-            tmem_wait_ld();
-            rs += vis ? pf_exp_half<T, false>(sv, h * 64, lim, p.scale_log2, m_use,
-                                              ptile + h * kPfHalf, (uint32_t)r, mx)
-                      : pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use,
-                                             ptile + h * kPfHalf, (uint32_t)r, mx);
-          }
-          redo = __any_sync(0xffffffffu, mx * p.scale_log2 > m_ref + kPfRescaleLog2);
-        }
-        if (redo) {
-          // first tile, or the max grew by more than 2^8 somewhere in the warp:
-          // take the exact row max, rescale O where needed, redo the exponentials
-          mx = -INFINITY;
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            float sv[64];
-            tmem_ld32(lane_addr + col_s + h * 64, sv);
-            tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 64; i += 2)
-              mx = fmax3(mx, h * 64 + i <= lim ? sv[i] : -INFINITY,
-                         h * 64 + i + 1 <= lim ? sv[i + 1] : -INFINITY);
-          }
-          const float m_new = fmaxf(m_ref, mx * p.scale_log2);
-          const bool need = m_new > m_ref + kPfRescaleLog2;
-          if (j >= 1 && __any_sync(0xffffffffu, need)) {
-            const float fac = need ? exp2f(m_ref - m_new) : 1.f;
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-              float o[16];
-              tmem_ld16(lane_addr + col_o + c * 16, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] *= fac;
-              tmem_st16(lane_addr + col_o + c * 16, o);
+          const int lim = lim_row - j * kPfBN;  // keys c <= lim are visible
+          // the whole warp sees every key of this tile: no masking needed
+          const bool vis = __all_sync(0xffffffffu, lim >= kPfBN - 1);
+          // PV_x(g-1) done: O_x is stable and the P_x tile is free (for j == 0
+          // the previous item's epilogue already waited for it)
+          if (j >= 1) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&o_done[x], pj ^ 1u, p.err))) {
+              alive = false;
+              break;
             }
-            tmem_wait_st();
-            l *= fac;
+            tc_fence_after();
           }
-          if (j == 0 || need) m_ref = m_new;
-          const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-          rs = 0.f;
-          float mx2 = -INFINITY;
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            float sv[64];
-            tmem_ld32(lane_addr + col_s + h * 64, sv);
-            tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
-            tmem_wait_ld();
-            rs += pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use, ptile + h * kPfHalf,
-                                       (uint32_t)r, mx2);
+          float rs = 0.f, mx = -INFINITY;
+          bool redo = (j == 0);
+          if (!redo) {
+            // one pass with the current reference max m_ref (exponentials <= 2^8
+            // unless the row max jumped, which the check below catches)
+            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+  #pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              float sv[64];
+              tmem_ld32(lane_addr + col_s + h * 64, sv);
+              tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
+              tmem_wait_ld();
+              rs += vis ? pf_exp_half<T, false>(sv, h * 64, lim, p.scale_log2, m_use,
+                                                ptile + h * kPfHalf, (uint32_t)r, mx)
+                        : pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use,
+                                               ptile + h * kPfHalf, (uint32_t)r, mx);
+            }
+            redo = __any_sync(0xffffffffu, mx * p.scale_log2 > m_ref + kPfRescaleLog2);
           }
+          if (redo) {
+            // first tile, or the max grew by more than 2^8 somewhere in the warp:
+            // take the exact row max, rescale O where needed, redo the exponentials
+            mx = -INFINITY;
+  #pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              float sv[64];
+              tmem_ld32(lane_addr + col_s + h * 64, sv);
+              tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
+              tmem_wait_ld();
+  #pragma unroll
+              for (int i = 0; i < 64; i += 2)
+                mx = fmax3(mx, h * 64 + i <= lim ? sv[i] : -INFINITY,
+                           h * 64 + i + 1 <= lim ? sv[i + 1] : -INFINITY);
+            }
+            const float m_new = fmaxf(m_ref, mx * p.scale_log2);
+            const bool need = m_new > m_ref + kPfRescaleLog2;
+            if (j >= 1 && __any_sync(0xffffffffu, need)) {
+              const float fac = need ? exp2f(m_ref - m_new) : 1.f;
+  #pragma unroll 1
+              for (int c = 0; c < 8; ++c) {
+                float o[16];
+                tmem_ld16(lane_addr + col_o + c * 16, o);
+                tmem_wait_ld();
+  #pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] *= fac;
+                tmem_st16(lane_addr + col_o + c * 16, o);
+              }
+              tmem_wait_st();
+              l *= fac;
+            }
+            if (j == 0 || need) m_ref = m_new;
+            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+            rs = 0.f;
+            float mx2 = -INFINITY;
+  #pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              float sv[64];
+              tmem_ld32(lane_addr + col_s + h * 64, sv);
+              tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
+              tmem_wait_ld();
+              rs += pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use, ptile + h * kPfHalf,
+                                         (uint32_t)r, mx2);
+            }
+          }
+          // S_x fully read: release it to the next S MMA
+          tc_fence_before();
+          mbar_arrive(&s_free[x]);
+          l += rs;
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(&p_full[x]);
         }
-        // S_x fully read: release it to the next S MMA
-        tc_fence_before();
-        mbar_arrive(&s_free[x]);
-        l += rs;
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&p_full[x]);
-      }
-      if (alive && ntiles > 0 &&
-          __all_sync(0xffffffffu, mbar_wait(&o_done[x], (uint32_t)(ntiles - 1) & 1u, p.err))) {
+        // the item's last PV_x: O_x complete
+        if (!alive ||
+            !__all_sync(0xffffffffu, mbar_wait(&o_done[x], (g - 1u) & 1u, p.err))) {
+          alive = false;
+          break;
+        }
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         T* dst = reinterpret_cast<T*>(p.out) +
-                 ((int64_t)(qs + qi) * p.num_q_heads + head0 + x) * kPfD;
+                 ((int64_t)(it.qs + qi) * p.num_q_heads + it.head0 + x) * kPfD;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float o[32];
           tmem_ld32(lane_addr + col_o + c * 32, o);
           tmem_wait_ld();
-          if (qi < q_len) {
+          if (qi < it.q_len) {
 #pragma unroll
             for (int d = 0; d < 32; d += 8) {
-              uint4 w;
-              w.x = DT<T>::from_f2(o[d] * inv, o[d + 1] * inv);
-              w.y = DT<T>::from_f2(o[d + 2] * inv, o[d + 3] * inv);
-              w.z = DT<T>::from_f2(o[d + 4] * inv, o[d + 5] * inv);
-              w.w = DT<T>::from_f2(o[d + 6] * inv, o[d + 7] * inv);
-              *reinterpret_cast<uint4*>(dst + c * 32 + d) = w;
+              uint4 wv;
+              wv.x = DT<T>::from_f2(o[d] * inv, o[d + 1] * inv);
+              wv.y = DT<T>::from_f2(o[d + 2] * inv, o[d + 3] * inv);
+              wv.z = DT<T>::from_f2(o[d + 4] * inv, o[d + 5] * inv);
+              wv.w = DT<T>::from_f2(o[d + 6] * inv, o[d + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + d) = wv;
             }
           }
         }
+        // O_x read (tcgen05.wait::ld above): the next item's first PV_x may
+        // overwrite it once this warpgroup arrives on p_full
       }
     }
   }
@@ -611,10 +679,17 @@ int launch_paged_prefill(const AttnArgs& a) {
   p.pair = (p.group % 2 == 0) ? 1 : 0;  // two heads of one kv group per CTA
   p.page_size = a.page;
   p.num_q_tiles = (a.max_q + kPfBM - 1) / kPfBM;
+  p.num_head_slots = p.pair ? a.hq / 2 : a.hq;
+  p.num_seqs = a.num_seqs;
+  const int64_t items = (int64_t)p.num_q_tiles * p.num_head_slots * a.num_seqs;
+  if (items > INT32_MAX) return set_error(NVKV_ERR_UNSUPPORTED, "paged prefill: too many tiles");
+  if (items == 0) return NVKV_OK;
+  p.num_items = (int)items;
   p.causal = a.causal;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = device_error_word();
-  dim3 grid(p.num_q_tiles, p.pair ? a.hq / 2 : a.hq, a.num_seqs);
+  // one persistent CTA per SM (the shared-memory footprint allows one)
+  const dim3 grid((unsigned)std::min<int64_t>(items, kPfCtas));
   if (a.dtype == NVKV_DTYPE_BF16) {
     auto kern = paged_prefill_kernel<__nv_bfloat16>;
     static unsigned long long attr_done_bf16 = 0;
