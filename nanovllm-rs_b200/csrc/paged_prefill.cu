@@ -296,9 +296,10 @@ __device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t sp, uint32
 
 // One work item = (q tile, head pair / head, sequence).  Items are numbered
 // q-tile-major with the heaviest causal tiles (last q tile) first, then head
-// slot, then sequence; CTA c takes items c, c + gridDim.x, ...  Returns 1 for
-// an item with work, 0 for an empty one (q_len <= 1: decode rows, or a tile
-// past q_len), -1 for a sequence with k_len < q_len (an error).
+// slot, then sequence; round k hands gridDim.x consecutive items to the CTAs
+// (pf_work).  Returns 1 for an item with work, 0 for an empty one (q_len <= 1:
+// decode rows, or a tile past q_len), -1 for a sequence with k_len < q_len
+// (an error).
 struct PfItem {
   int b, head0, kvh, i0, q_len, k_len, off, ntiles;
   uint32_t qs, ks;
@@ -323,6 +324,13 @@ __device__ __forceinline__ int pf_item(const PrefillParams& p, int w, PfItem& it
   const int kmax = p.causal ? min(it.k_len, last_row + it.off + 1) : it.k_len;
   it.ntiles = (kmax + kPfBN - 1) / kPfBN;
   return 1;
+}
+
+// Item of round k for this CTA: rounds alternate direction (snake order), so
+// the CTA that took a round's heaviest item takes the next round's lightest.
+__device__ __forceinline__ int pf_work(int k) {
+  const int c = (k & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
+  return k * (int)gridDim.x + c;
 }
 
 // Persistent: one CTA per SM walks its items with the barriers, TMEM and
@@ -387,7 +395,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma_prefetch_desc(&tmap_v);
       uint32_t nq = 0, t = 0;  // items loaded, K/V ring loads (running over items)
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < p.num_items; w += gridDim.x) {
+      for (int k = 0; ok && (int64_t)k * gridDim.x < p.num_items; ++k) {
+        const int w = pf_work(k);
+        if (w >= p.num_items) continue;
         PfItem it;
         const int kind = pf_item(p, w, it);
         if (kind < 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
@@ -442,7 +452,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #define PF_FULL(t) (&kv_full[(t) % kPfSlots])
       uint32_t nq = 0, t = 0, g = 0;  // items, K/V ring position, key tiles per slot
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < p.num_items; w += gridDim.x) {
+      for (int k = 0; ok && (int64_t)k * gridDim.x < p.num_items; ++k) {
+        const int w = pf_work(k);
+        if (w >= p.num_items) continue;
         PfItem it;
         if (pf_item(p, w, it) <= 0) continue;
         const int n = it.ntiles;
@@ -516,7 +528,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       uint8_t* ptile = smem + (x ? kPfOffPB : kPfOffPA);
       uint32_t g = 0;  // key tiles of this slot so far (running over items)
       bool alive = true;
-      for (int w = blockIdx.x; alive && w < p.num_items; w += gridDim.x) {
+      for (int k = 0; alive && (int64_t)k * gridDim.x < p.num_items; ++k) {
+        const int w = pf_work(k);
+        if (w >= p.num_items) continue;
         PfItem it;
         if (pf_item(p, w, it) <= 0) continue;
         const int qi = it.i0 + r;
@@ -682,7 +696,8 @@ int launch_paged_prefill(const AttnArgs& a) {
   p.num_head_slots = p.pair ? a.hq / 2 : a.hq;
   p.num_seqs = a.num_seqs;
   const int64_t items = (int64_t)p.num_q_tiles * p.num_head_slots * a.num_seqs;
-  if (items > INT32_MAX) return set_error(NVKV_ERR_UNSUPPORTED, "paged prefill: too many tiles");
+  if (items > INT32_MAX - kPfCtas)
+    return set_error(NVKV_ERR_UNSUPPORTED, "paged prefill: too many tiles");
   if (items == 0) return NVKV_OK;
   p.num_items = (int)items;
   p.causal = a.causal;
