@@ -5,12 +5,13 @@
 // layers/attention.rs:43-73; FA2 with SM80 mma.sync) for every sequence
 // whose q_len > 1 (q_len == 1 rows run on the decode kernel).
 //
-// One CTA = 128 query rows x TWO query heads of the same kv group (slots A
-// and B; one slot when the group size is odd).  Both slots read the same K/V
-// tiles, so every K/V tile is fetched once per head pair, and the two
-// softmax warpgroups ping-pong against the tensor core.  10 warps:
-//   warp 0      TMA producer: Q_A/Q_B once, then K_j, V_j (128 keys each,
-//               pages resolved through block_tables) through a 3-slot ring,
+// One work item = 128 query rows x TWO query heads of the same kv group
+// (slots A and B; one slot when the group size is odd).  Both slots read the
+// same K/V tiles, so every K/V tile is fetched once per head pair, and the
+// two softmax warpgroups ping-pong against the tensor core.  The kernel is
+// persistent (one CTA per SM walking its work items, see pf_work).  10 warps:
+//   warp 0      TMA producer: Q_A/Q_B per item, then K_j, V_j (128 keys each,
+//               pages resolved through block_tables) through a 5-slot ring,
 //               SWIZZLE_128B, each CTA loading its own tiles;
 //   warp 1      allocates all 512 TMEM columns (S_A, S_B, O_A, O_B) and
 //               issues every tcgen05.mma.cta_group::1.kind::f16 from one
@@ -18,19 +19,23 @@
 //               so the tensor core computes one slot while the other slot's
 //               softmax runs; tcgen05.commit arrives on the mbarriers;
 //   warps 2-5   softmax warpgroup of slot A, warps 6-9 of slot B: thread r
-//               owns query row r (TMEM lane r).  Per key tile it reads its S
-//               row from TMEM in two passes of 64 columns (tcgen05.ld 32x32b;
-//               max first, then exponentials), masks (causal, bottom-right:
-//               key j visible to query i iff j <= i + k_len - q_len), takes
-//               the row max, and rescales the TMEM O row (tcgen05.ld/st) only
+//               owns query row r (TMEM lane r).  Per key tile it loads its
+//               whole S row from TMEM (four tcgen05.ld 32x32b.x32, one wait),
+//               masks (causal, bottom-right: key j visible to query i iff
+//               j <= i + k_len - q_len), takes the exact row max from
+//               registers, and rescales the TMEM O row (tcgen05.ld/st) only
 //               when the max grew by more than 2^8 -- otherwise it keeps the
 //               stale max, whose exponentials stay <= 256 and exact enough in
-//               fp32/bf16 -- then writes P = 2^(s*scale - m) into a swizzled
-//               K-major shared-memory tile.  The exponentials run on the
-//               MUFU ex2 unit; the scaling FMAs and the row sum use packed
-//               f32x2 instructions (the FMA pipe, not MUFU, is the busier
-//               one here: moving exponentials from a polynomial on the FMA
-//               pipe to MUFU measured 308 -> 272 us on the 8B prefill).
+//               fp32/bf16 -- then writes P = 2^(s*scale - m) as 16-bit pairs
+//               back into the first 64 columns of its S region (tcgen05.st).
+//               The P.V MMA takes P from TMEM as its A operand, so no shared
+//               memory holds P and the 64 KB it would take deepen the K/V
+//               ring; S_x(j+1) may overwrite P_x(j) because it is issued
+//               after PV_x(j) on the in-order tensor pipe.  The exponentials
+//               run on the MUFU ex2 unit; the scaling FMAs and the row sum
+//               use packed f32x2 instructions (the FMA pipe, not MUFU, is the
+//               busier one here: moving exponentials from a polynomial on the
+//               FMA pipe to MUFU measured 308 -> 272 us on the 8B prefill).
 //   O accumulates in TMEM across key tiles (PV MMAs chain with
 //   accumulate = 1); the epilogue divides by the row sum and stores bf16/f16.
 // Roofline: tensor cores; flops = 4 * D * (visible (query, key) pairs).
@@ -44,17 +49,15 @@ namespace nvkv {
 constexpr int kPfD = 128;
 constexpr int kPfBM = 128;
 constexpr int kPfBN = 128;
-constexpr int kPfSlots = 3;                 // K/V ring: K_j and V_j each take one slot
+constexpr int kPfSlots = 5;                 // K/V ring: K_j and V_j each take one slot
 constexpr int kPfThreads = 10 * 32;
 constexpr int kPfHalf = 128 * 128;          // 128 rows x 128 B (64 elements)
 constexpr int kPfTile = 2 * kPfHalf;        // 32 KB: 128 rows x 128 elements
 constexpr int kPfOffQA = 0;
 constexpr int kPfOffQB = kPfOffQA + kPfTile;
 constexpr int kPfOffKV = kPfOffQB + kPfTile;
-constexpr int kPfOffPA = kPfOffKV + kPfSlots * kPfTile;
-constexpr int kPfOffPB = kPfOffPA + kPfTile;
-constexpr int kPfOffBar = kPfOffPB + kPfTile;
-constexpr int kPfNumBars = 2 + 2 * kPfSlots + 8;
+constexpr int kPfOffBar = kPfOffKV + kPfSlots * kPfTile;
+constexpr int kPfNumBars = 2 + 2 * kPfSlots + 6;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfCtas = 148;  // B200 SMs
@@ -116,9 +119,6 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -215,6 +215,16 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+// D (+)= A.B with A read from tensor memory (the P tile), B from shared memory.
+__device__ __forceinline__ void tc_mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bit.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
@@ -235,38 +245,23 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
 }
 
 // P for one 64-key half of a row: e = 2^(s*scale - m) (masked keys -> 0) on
-// the MUFU unit, packed into the swizzled K-major tile; returns the sum of
-// the e values and folds the half's max of s into `mx`.
+// the MUFU unit, packed in pairs into pk[32] (the half's 32 TMEM columns of
+// 16-bit pairs); returns the sum of the e values.
 template <typename T, bool kMask>
 __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim, float scale_log2,
-                                             float m_use, uint8_t* half, uint32_t row,
-                                             float& mx) {
+                                             float m_use, uint32_t* pk) {
   uint64_t rs2 = f2_pack(0.f, 0.f);  // the row sum in two packed lanes
   const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_use, -m_use);
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    uint32_t pk[4];
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const int i = u * 8 + e;
-      float s0 = sv[i], s1 = sv[i + 1];
-      if (kMask) {
-        s0 = kbase + i <= lim ? s0 : -INFINITY;
-        s1 = kbase + i + 1 <= lim ? s1 : -INFINITY;
-      }
-      mx = fmax3(mx, s0, s1);
-      const float2 xx = f2_unpack(f2_fma(f2_pack(s0, s1), sc2, nm2));
-      const float x0 = xx.x, x1 = xx.y;
-      float e0 = ex2_mufu(x0), e1 = ex2_mufu(x1);
-      if (kMask) {
-        e0 = kbase + i <= lim ? e0 : 0.f;
-        e1 = kbase + i + 1 <= lim ? e1 : 0.f;
-      }
-      rs2 = f2_add(rs2, f2_pack(e0, e1));
-      pk[e >> 1] = pack_p<T>(e0, e1);
+  for (int i = 0; i < 64; i += 2) {
+    const float2 xx = f2_unpack(f2_fma(f2_pack(sv[i], sv[i + 1]), sc2, nm2));
+    float e0 = ex2_mufu(xx.x), e1 = ex2_mufu(xx.y);
+    if (kMask) {
+      e0 = kbase + i <= lim ? e0 : 0.f;
+      e1 = kbase + i + 1 <= lim ? e1 : 0.f;
     }
-    *reinterpret_cast<uint4*>(half + sw128_offset(row, (uint32_t)u)) =
-        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    rs2 = f2_add(rs2, f2_pack(e0, e1));
+    pk[i >> 1] = pack_p<T>(e0, e1);
   }
   const float2 rs = f2_unpack(rs2);
   return rs.x + rs.y;
@@ -282,15 +277,16 @@ __device__ __forceinline__ void pf_issue_s(uint32_t d_tmem, uint32_t sq, uint32_
     tc_mma(d_tmem, sdesc(sq + o, 16, 1024), sdesc(sk + o, 16, 1024), idesc, kk > 0 ? 1u : 0u);
   }
 }
-// O_x (+)= P_x . V over 128 keys: P K-major (keys in 64-key halves), V MN-major
-// (D contiguous, the two 64-wide D halves kPfHalf apart = LBO, 8 keys = SBO).
-__device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t sp, uint32_t sv,
+// O_x (+)= P_x . V over 128 keys: P_x in TMEM (lane = query row, 64 columns of
+// 16-bit key pairs over the S_x columns), 16 keys = 8 columns per MMA; V
+// MN-major in shared memory (D contiguous, the two 64-wide D halves kPfHalf
+// apart = LBO, 8 keys = SBO).
+__device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv,
                                             uint32_t idesc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < kPfBN / 16; ++kk) {
-    const uint64_t ad = sdesc(sp + (kk >> 2) * kPfHalf + (kk & 3) * 32, 16, 1024);
     const uint64_t bd = sdesc(sv + kk * 16 * 128, kPfHalf, 1024);
-    tc_mma(d_tmem, ad, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
+    tc_mma_tmem_a(d_tmem, p_tmem + kk * 8, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
@@ -355,8 +351,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* kv_full = bars + 2;             // [kPfSlots]
   uint64_t* kv_empty = kv_full + kPfSlots;  // [kPfSlots]
   uint64_t* s_full = kv_empty + kPfSlots;   // [2]: S_x written by the MMA
-  uint64_t* s_free = s_full + 2;            // [2]: S_x read by its softmax warpgroup
-  uint64_t* p_full = s_free + 2;            // [2]: P_x written (and O_x rescaled / read)
+  uint64_t* p_full = s_full + 2;            // [2]: S_x read, P_x written (O_x rescaled / read)
   uint64_t* o_done = p_full + 2;            // [2]: PV_x finished (O_x stable, P_x free)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
@@ -372,7 +367,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
-      mbar_init(&s_free[x], 128);
       mbar_init(&p_full[x], 128);
       mbar_init(&o_done[x], 1);
     }
@@ -446,7 +440,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       constexpr uint32_t idesc_pv = make_idesc(fmt, 1u);
       const uint32_t kv0 = smem_u32(smem + kPfOffKV);
       const uint32_t sqa = smem_u32(smem + kPfOffQA), sqb = smem_u32(smem + kPfOffQB);
-      const uint32_t spa = smem_u32(smem + kPfOffPA), spb = smem_u32(smem + kPfOffPB);
 #define PF_SLOT(t) (kv0 + (uint32_t)((t) % kPfSlots) * kPfTile)
 #define PF_PAR(t) ((uint32_t)((t) / kPfSlots) & 1u)
 #define PF_FULL(t) (&kv_full[(t) % kPfSlots])
@@ -458,17 +451,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         PfItem it;
         if (pf_item(p, w, it) <= 0) continue;
         const int n = it.ntiles;
-        // S_x(g) of the item's first key tile: Q, K_0, and S_x(g - 1) read
-        ok = mbar_wait(q_full, nq & 1u, p.err) && mbar_wait(PF_FULL(t), PF_PAR(t), p.err) &&
-             (g == 0 || mbar_wait(&s_free[0], (g - 1) & 1u, p.err));
+        // S_x(g) of the item's first key tile: Q and K_0 (S_x / P_x(g - 1) were
+        // consumed by PV_x(g - 1), issued before it on the in-order pipe)
+        ok = mbar_wait(q_full, nq & 1u, p.err) && mbar_wait(PF_FULL(t), PF_PAR(t), p.err);
         if (!ok) break;
         tc_fence_after();
         pf_issue_s(tmem + 0u, sqa, PF_SLOT(t), idesc_qk);
         tc_commit(&s_full[0]);
         if (p.pair) {
-          ok = g == 0 || mbar_wait(&s_free[1], (g - 1) & 1u, p.err);
-          if (!ok) break;
-          tc_fence_after();
           pf_issue_s(tmem + 128u, sqb, PF_SLOT(t), idesc_qk);
           tc_commit(&s_full[1]);
         }
@@ -482,10 +472,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           ok = mbar_wait(PF_FULL(tv), PF_PAR(tv), p.err) && mbar_wait(&p_full[0], pj, p.err);
           if (!ok) break;
           tc_fence_after();
-          pf_issue_pv(tmem + 256u, spa, PF_SLOT(tv), idesc_pv, j > 0);
+          pf_issue_pv(tmem + 256u, tmem + 0u, PF_SLOT(tv), idesc_pv, j > 0);
           tc_commit(&o_done[0]);
           if (more) {
-            ok = mbar_wait(PF_FULL(tk), PF_PAR(tk), p.err) && mbar_wait(&s_free[0], pj, p.err);
+            ok = mbar_wait(PF_FULL(tk), PF_PAR(tk), p.err);
             if (!ok) break;
             tc_fence_after();
             pf_issue_s(tmem + 0u, sqa, PF_SLOT(tk), idesc_qk);
@@ -495,15 +485,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             ok = mbar_wait(&p_full[1], pj, p.err);
             if (!ok) break;
             tc_fence_after();
-            pf_issue_pv(tmem + 384u, spb, PF_SLOT(tv), idesc_pv, j > 0);
+            pf_issue_pv(tmem + 384u, tmem + 128u, PF_SLOT(tv), idesc_pv, j > 0);
             tc_commit(&o_done[1]);
           }
           tc_commit(&kv_empty[tv % kPfSlots]);  // V_j: both P.V issued
           if (more) {
             if (p.pair) {
-              ok = mbar_wait(&s_free[1], pj, p.err);
-              if (!ok) break;
-              tc_fence_after();
               pf_issue_s(tmem + 128u, sqb, PF_SLOT(tk), idesc_qk);
               tc_commit(&s_full[1]);
             }
@@ -525,7 +512,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int r = quarter * 32 + lane;
       const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
       const uint32_t col_s = x ? 128u : 0u, col_o = x ? 384u : 256u;
-      uint8_t* ptile = smem + (x ? kPfOffPB : kPfOffPA);
       uint32_t g = 0;  // key tiles of this slot so far (running over items)
       bool alive = true;
       for (int k = 0; alive && (int64_t)k * gridDim.x < p.num_items; ++k) {
@@ -538,7 +524,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         float m_ref = -INFINITY, l = 0.f;
         for (int j = 0; j < it.ntiles; ++j, ++g) {
           const uint32_t pj = g & 1u;
-          // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned
+          // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned.
+          // s_full(g) also means PV_x(g - 1) is complete (it was issued before
+          // S_x(g)): O_x is stable for a rescale.
           if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], pj, p.err))) {
             alive = false;
             break;
@@ -547,84 +535,59 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const int lim = lim_row - j * kPfBN;  // keys c <= lim are visible
           // the whole warp sees every key of this tile: no masking needed
           const bool vis = __all_sync(0xffffffffu, lim >= kPfBN - 1);
-          // PV_x(g-1) done: O_x is stable and the P_x tile is free (for j == 0
-          // the previous item's epilogue already waited for it)
-          if (j >= 1) {
-            if (!__all_sync(0xffffffffu, mbar_wait(&o_done[x], pj ^ 1u, p.err))) {
-              alive = false;
-              break;
-            }
-            tc_fence_after();
+          // the whole S row in registers: one TMEM round trip, exact tile max
+          float sv[128];
+          tmem_ld32(lane_addr + col_s, sv);
+          tmem_ld32(lane_addr + col_s + 32, sv + 32);
+          tmem_ld32(lane_addr + col_s + 64, sv + 64);
+          tmem_ld32(lane_addr + col_s + 96, sv + 96);
+          tmem_wait_ld();
+          float mx = -INFINITY;
+          if (vis) {
+#pragma unroll
+            for (int i = 0; i < 128; i += 2) mx = fmax3(mx, sv[i], sv[i + 1]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 128; i += 2)
+              mx = fmax3(mx, i <= lim ? sv[i] : -INFINITY, i + 1 <= lim ? sv[i + 1] : -INFINITY);
           }
-          float rs = 0.f, mx = -INFINITY;
-          bool redo = (j == 0);
-          if (!redo) {
-            // one pass with the current reference max m_ref (exponentials <= 2^8
-            // unless the row max jumped, which the check below catches)
-            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-  #pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              float sv[64];
-              tmem_ld32(lane_addr + col_s + h * 64, sv);
-              tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
-              tmem_wait_ld();
-              rs += vis ? pf_exp_half<T, false>(sv, h * 64, lim, p.scale_log2, m_use,
-                                                ptile + h * kPfHalf, (uint32_t)r, mx)
-                        : pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use,
-                                               ptile + h * kPfHalf, (uint32_t)r, mx);
-            }
-            redo = __any_sync(0xffffffffu, mx * p.scale_log2 > m_ref + kPfRescaleLog2);
+          // keep the reference max unless the row max grew by more than 2^8
+          // (exponentials stay <= 256); then the TMEM O row is rescaled below
+          const float m_new = fmaxf(m_ref, mx * p.scale_log2);
+          const bool need = m_new > m_ref + kPfRescaleLog2;
+          const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
+          const float fac = need ? exp2f(m_ref - m_new) : 1.f;
+          if (j == 0 || need) m_ref = m_new;
+          const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+          // P_x over the S_x columns just read: keys 0-63 -> columns 0-31,
+          // keys 64-127 -> columns 32-63 (the PV MMA's A operand)
+          float rs;
+          {
+            uint32_t pk[32];
+            rs = vis ? pf_exp_half<T, false>(sv, 0, lim, p.scale_log2, m_use, pk)
+                     : pf_exp_half<T, true>(sv, 0, lim, p.scale_log2, m_use, pk);
+            tmem_st32(lane_addr + col_s, reinterpret_cast<const float*>(pk));
           }
-          if (redo) {
-            // first tile, or the max grew by more than 2^8 somewhere in the warp:
-            // take the exact row max, rescale O where needed, redo the exponentials
-            mx = -INFINITY;
-  #pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              float sv[64];
-              tmem_ld32(lane_addr + col_s + h * 64, sv);
-              tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
-              tmem_wait_ld();
-  #pragma unroll
-              for (int i = 0; i < 64; i += 2)
-                mx = fmax3(mx, h * 64 + i <= lim ? sv[i] : -INFINITY,
-                           h * 64 + i + 1 <= lim ? sv[i + 1] : -INFINITY);
-            }
-            const float m_new = fmaxf(m_ref, mx * p.scale_log2);
-            const bool need = m_new > m_ref + kPfRescaleLog2;
-            if (j >= 1 && __any_sync(0xffffffffu, need)) {
-              const float fac = need ? exp2f(m_ref - m_new) : 1.f;
-  #pragma unroll 1
-              for (int c = 0; c < 8; ++c) {
-                float o[16];
-                tmem_ld16(lane_addr + col_o + c * 16, o);
-                tmem_wait_ld();
-  #pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] *= fac;
-                tmem_st16(lane_addr + col_o + c * 16, o);
-              }
-              tmem_wait_st();
-              l *= fac;
-            }
-            if (j == 0 || need) m_ref = m_new;
-            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-            rs = 0.f;
-            float mx2 = -INFINITY;
-  #pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              float sv[64];
-              tmem_ld32(lane_addr + col_s + h * 64, sv);
-              tmem_ld32(lane_addr + col_s + h * 64 + 32, sv + 32);
-              tmem_wait_ld();
-              rs += pf_exp_half<T, true>(sv, h * 64, lim, p.scale_log2, m_use, ptile + h * kPfHalf,
-                                         (uint32_t)r, mx2);
-            }
+          {
+            uint32_t pk[32];
+            rs += vis ? pf_exp_half<T, false>(sv + 64, 64, lim, p.scale_log2, m_use, pk)
+                      : pf_exp_half<T, true>(sv + 64, 64, lim, p.scale_log2, m_use, pk);
+            tmem_st32(lane_addr + col_s + 32, reinterpret_cast<const float*>(pk));
           }
-          // S_x fully read: release it to the next S MMA
-          tc_fence_before();
-          mbar_arrive(&s_free[x]);
+          if (rescale) {  // O_x *= 2^(m_old - m_new) before PV_x(g) adds to it
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {
+              float o[16];
+              tmem_ld16(lane_addr + col_o + c * 16, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] *= fac;
+              tmem_st16(lane_addr + col_o + c * 16, o);
+            }
+            l *= fac;
+          }
+          tmem_wait_st();
           l += rs;
-          fence_proxy_async_smem();
           tc_fence_before();
           mbar_arrive(&p_full[x]);
         }

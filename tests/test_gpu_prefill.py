@@ -14,11 +14,15 @@ from helpers import assert_attention_close, cu, f32, gather_seq, make_paged
 pytestmark = pytest.mark.gpu
 
 
-def _contiguous_case(lens, hq, hkv, dtype=torch.bfloat16, causal=True, seed=0):
+def _contiguous_case(lens, hq, hkv, dtype=torch.bfloat16, causal=True, seed=0, k_gain=None):
     g = torch.Generator().manual_seed(seed)
     d, T = 128, sum(lens)
     q = torch.randn(T, hq, d, generator=g).to(dtype).cuda()
-    k = torch.randn(T, hkv, d, generator=g).to(dtype).cuda()
+    k = torch.randn(T, hkv, d, generator=g)
+    if k_gain is not None:  # per-position key scale: k[t] *= k_gain(position in its sequence)
+        pos = np.concatenate([np.arange(L) for L in lens])
+        k = k * torch.from_numpy(k_gain(pos).astype(np.float32))[:, None, None]
+    k = k.to(dtype).cuda()
     v = torch.randn(T, hkv, d, generator=g).to(dtype).cuda()
     scale = d ** -0.5
     out = nvkv.paged_attention(q, k, v, cu(lens), cu(lens), None, max(lens), max(lens), scale,
@@ -41,6 +45,15 @@ def test_prefill_pure_causal(lens):
 @pytest.mark.parametrize("group", [1, 4, 8])
 def test_prefill_gqa_groups(group):
     _contiguous_case([200, 77], 2 * group, 2, seed=group)
+
+
+def test_prefill_row_max_growth_rescales():
+    """Scores that keep growing along the keys: the row max rises by far more
+    than 2^8 (the lazy-rescale threshold) from one 128-key tile to the next,
+    so the kernel must rescale O and the row sum on most tiles."""
+    _contiguous_case([700, 300], 4, 2, seed=11, k_gain=lambda pos: 1.0 + pos / 64.0)
+    _contiguous_case([520], 4, 1, dtype=torch.float16, seed=12,
+                     k_gain=lambda pos: np.where(pos >= 256, 6.0, 1.0))
 
 
 def test_prefill_f16_and_noncausal():
