@@ -31,11 +31,10 @@
 //               The P.V MMA takes P from TMEM as its A operand, so no shared
 //               memory holds P and the 64 KB it would take deepen the K/V
 //               ring; S_x(j+1) may overwrite P_x(j) because it is issued
-//               after PV_x(j) on the in-order tensor pipe.  The exponentials
-//               run on the MUFU ex2 unit; the scaling FMAs and the row sum
-//               use packed f32x2 instructions (the FMA pipe, not MUFU, is the
-//               busier one here: moving exponentials from a polynomial on the
-//               FMA pipe to MUFU measured 308 -> 272 us on the 8B prefill).
+//               after PV_x(j) on the in-order tensor pipe.  Seven exponential
+//               pairs in eight run on the MUFU ex2 unit, one on a polynomial
+//               on the FMA pipe (kPfPolyEvery); the scaling FMAs and the row
+//               sum use packed f32x2 instructions.
 //   O accumulates in TMEM across key tiles (PV MMAs chain with
 //   accumulate = 1); the epilogue divides by the row sum and stores bf16/f16.
 // Roofline: tensor cores; flops = 4 * D * (visible (query, key) pairs).
@@ -61,7 +60,15 @@ constexpr int kPfNumBars = 2 + 2 * kPfSlots + 6;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfCtas = 148;  // B200 SMs
-constexpr float kPfRescaleLog2 = 8.0f;  // rescale O only when the max grows by > 2^8
+constexpr float kPfRescaleLog2 = 8.0f;
+// One exponential pair in NVKV_PF_POLY_EVERY runs on the FMA-pipe polynomial
+// instead of MUFU ex2 (0: all on MUFU), balancing the two pipes.  Measured on
+// the 8B prefill (16 x 1024, causal): 0 -> 207 us, 16 -> 208, 10 -> 202,
+// 8 -> 197.5, 6 -> 199, 4 -> 204, 2 -> 217.
+#ifndef NVKV_PF_POLY_EVERY
+#define NVKV_PF_POLY_EVERY 8
+#endif
+constexpr int kPfPolyEvery = NVKV_PF_POLY_EVERY;  // rescale O only when the max grows by > 2^8
 
 static_assert(kPfSmemBytes <= 232448, "prefill shared memory exceeds 227 KB");
 
@@ -185,6 +192,13 @@ __device__ __forceinline__ float ex2_mufu(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for two values on the FMA pipe: x = n + f with n = round(x), f in
+// [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here to the exact function
+// (max relative error 7.5e-5, far below bf16's 2^-9 half-ulp); 2^n is added
+// into the exponent bits.  The adds and FMAs are issued as packed f32x2
+// pairs.  Valid for x in [-125, 126]; smaller x is clamped (the result,
+// ~2^-125, is negligible next to the row sum it joins); NaN inputs clamp too.
+__device__ __forceinline__ float2 ex2_poly2(float x0, float x1);
 // max(a, b, c) in one instruction (three-input PTX max.f32; NaN handling as
 // fmaxf: a NaN operand is ignored).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -225,6 +239,25 @@ __device__ __forceinline__ void tc_mma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, 
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const uint64_t x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = f2_add(x, magic);  // t's low mantissa bits hold round(x)
+  const float2 tv = f2_unpack(t);
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));
+  uint64_t q = f2_fma(f2_pack(0.05517153f, 0.05517153f), f, f2_pack(0.24261111f, 0.24261111f));
+  q = f2_fma(q, f, f2_pack(0.69326103f, 0.69326103f));
+  q = f2_fma(q, f, f2_pack(0.99992806f, 0.99992806f));
+  const float2 qv = f2_unpack(q);
+  const int n0 = __float_as_int(tv.x) - 0x4B400000, n1 = __float_as_int(tv.y) - 0x4B400000;
+  return make_float2(__int_as_float(__float_as_int(qv.x) + (n0 << 23)),
+                     __int_as_float(__float_as_int(qv.y) + (n1 << 23)));
+}
 // Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bit.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
@@ -255,7 +288,15 @@ __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim
 #pragma unroll
   for (int i = 0; i < 64; i += 2) {
     const float2 xx = f2_unpack(f2_fma(f2_pack(sv[i], sv[i + 1]), sc2, nm2));
-    float e0 = ex2_mufu(xx.x), e1 = ex2_mufu(xx.y);
+    float e0, e1;
+    if (kPfPolyEvery > 0 && (i / 2) % (kPfPolyEvery > 0 ? kPfPolyEvery : 1) == kPfPolyEvery - 1) {
+      const float2 ee = ex2_poly2(xx.x, xx.y);  // this pair on the FMA pipe
+      e0 = ee.x;
+      e1 = ee.y;
+    } else {
+      e0 = ex2_mufu(xx.x);
+      e1 = ex2_mufu(xx.y);
+    }
     if (kMask) {
       e0 = kbase + i <= lim ? e0 : 0.f;
       e1 = kbase + i + 1 <= lim ? e1 : 0.f;
@@ -542,15 +583,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tmem_ld32(lane_addr + col_s + 64, sv + 64);
           tmem_ld32(lane_addr + col_s + 96, sv + 96);
           tmem_wait_ld();
-          float mx = -INFINITY;
+          // four independent max chains, then combined
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
           if (vis) {
 #pragma unroll
-            for (int i = 0; i < 128; i += 2) mx = fmax3(mx, sv[i], sv[i + 1]);
+            for (int i = 0; i < 128; i += 2) m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], sv[i], sv[i + 1]);
           } else {
 #pragma unroll
             for (int i = 0; i < 128; i += 2)
-              mx = fmax3(mx, i <= lim ? sv[i] : -INFINITY, i + 1 <= lim ? sv[i + 1] : -INFINITY);
+              m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], i <= lim ? sv[i] : -INFINITY,
+                                       i + 1 <= lim ? sv[i + 1] : -INFINITY);
           }
+          const float mx = fmaxf(fmax3(m4[0], m4[1], m4[2]), m4[3]);
           // keep the reference max unless the row max grew by more than 2^8
           // (exponentials stay <= 256); then the TMEM O row is rescaled below
           const float m_new = fmaxf(m_ref, mx * p.scale_log2);
