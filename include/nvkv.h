@@ -141,7 +141,10 @@ int nvkv_qknorm_rope(const void* qkv, int64_t qkv_stride, int64_t num_tokens, in
  * tcgen05 prefill kernel.  max_seqlen_q/k bound the per-sequence lengths.
  * D must be 128; Hq % Hkv == 0 with Hq/Hkv <= 16; page_size a multiple of
  * 128.  `workspace` must hold nvkv_paged_attention_workspace_size() bytes
- * (16-byte aligned); it may be NULL when that size is 0.
+ * (16-byte aligned); it may be NULL when that size is 0.  It holds the
+ * split-KV scratch and, when max_seqlen_q > 1, the prefill work plan (a
+ * sort of the q_len > 1 sequences by q-tile count, about 4 * (num_seqs +
+ * max_seqlen_q / 128) bytes), rebuilt by every call.
  * ---------------------------------------------------------------------- */
 int nvkv_paged_attention_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
                                         int head_dim, int max_seqlen_q, int max_seqlen_k,
@@ -163,8 +166,8 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
  * all free GPU memory to its KV pool, code inside a stream capture that may
  * not allocate, a binding with no allocator at hand).  No counterpart in the
  * reference: its flash-attn call allocates through candle.
- * Same inputs, outputs and validation as nvkv_paged_attention.  The split-KV
- * scratch is a file-scope device array of NVKV_NOALLOC_SCRATCH_BYTES held by
+ * Same inputs, outputs and validation as nvkv_paged_attention.  The
+ * workspace (split-KV scratch and prefill plan) is a file-scope device array of NVKV_NOALLOC_SCRATCH_BYTES held by
  * every GPU that loads the library until exit; batches whose plan needs more
  * are rejected with NVKV_ERR_WORKSPACE.  All calls share that array (it keeps
  * the last call's contents; nothing needs to start zeroed), so calls that

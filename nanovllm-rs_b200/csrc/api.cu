@@ -24,6 +24,14 @@ static int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, 
   return NVKV_OK;
 }
 
+// Split-KV decode scratch, then (for max_seqlen_q > 1) the prefill work plan.
+static size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k) {
+  if (num_seqs <= 0) return 0;
+  const size_t dec = decode_workspace_bytes(num_seqs, hq, hkv, max_k);
+  const size_t plan = prefill_plan_bytes(num_seqs, max_q);
+  return plan ? attention_plan_offset(dec) + plan : dec;
+}
+
 static int run_attention(const AttnArgs& a) {
   int rc = launch_paged_decode(a);
   if (rc) return rc;
@@ -98,9 +106,8 @@ int nvkv_paged_attention_workspace_size(int num_seqs, int num_q_heads, int num_k
   int rc = validate_shapes(num_seqs, max_seqlen_q, max_seqlen_k, num_q_heads, num_kv_heads,
                            head_dim);
   if (rc) return rc;
-  *bytes = num_seqs > 0 ? decode_workspace_bytes(num_seqs, num_q_heads, num_kv_heads,
-                                                 max_seqlen_k)
-                        : 0;
+  *bytes = attention_workspace_bytes(num_seqs, num_q_heads, num_kv_heads, max_seqlen_q,
+                                     max_seqlen_k);
   return NVKV_OK;
 }
 
@@ -149,7 +156,8 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
                      "paged_attention: q/k_cache/v_cache/out and q_stride must be 16-byte aligned");
   if (!(softmax_scale > 0.f))
     return set_error(NVKV_ERR_INVALID_ARG, "paged_attention: softmax_scale must be > 0");
-  const size_t need = decode_workspace_bytes(num_seqs, num_q_heads, num_kv_heads, max_seqlen_k);
+  const size_t need =
+      attention_workspace_bytes(num_seqs, num_q_heads, num_kv_heads, max_seqlen_q, max_seqlen_k);
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned16(workspace)))
     return set_error(NVKV_ERR_WORKSPACE, "paged_attention: workspace missing or too small (need " +
                                              std::to_string(need) + " bytes)");

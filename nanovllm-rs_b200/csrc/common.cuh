@@ -77,6 +77,11 @@ size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, i
 void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
                  int* max_splits);
 int launch_paged_prefill(const AttnArgs& a);
+// Bytes of the prefill work plan (0 when max_seqlen_q <= 1); it sits in the
+// attention workspace after the decode scratch, at attention_plan_offset().
+size_t prefill_plan_bytes(int num_seqs, int max_seqlen_q);
+inline size_t attention_plan_offset(size_t decode_bytes) { return (decode_bytes + 255) & ~size_t(255); }
+constexpr int kPfMaxQTiles = 12000;  // plan histogram in 48 KB of shared memory
 int launch_store_kvcache(const void* key, const void* value, void* k_cache, void* v_cache,
                          const int64_t* slot_mapping, int64_t num_tokens, int64_t row_elems,
                          int64_t key_stride, int64_t value_stride, int64_t num_slots,

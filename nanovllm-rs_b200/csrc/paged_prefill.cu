@@ -60,6 +60,12 @@ constexpr int kPfNumBars = 2 + 2 * kPfSlots + 6;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfCtas = 148;  // B200 SMs
+// Candidate items per CTA up to which the kernel enumerates every (q tile,
+// head slot, sequence) instead of building a work plan first (measured on the
+// 8B prefill, 16 x 1024: 197 us direct against 212 us with the plan; a mixed
+// step of 120 decodes + 8 prompts, 221 candidates per CTA: 362 us direct
+// against 265 us with the plan).
+constexpr int kPfDirectItemsPerCta = 32;
 constexpr float kPfRescaleLog2 = 8.0f;
 // One exponential pair in NVKV_PF_POLY_EVERY runs on the FMA-pipe polynomial
 // instead of MUFU ex2 (0: all on MUFU), balancing the two pipes.  Measured on
@@ -84,9 +90,16 @@ struct PrefillParams {
   int pair;  // 1: slots A/B are heads 2p, 2p+1 of one kv group; 0: slot A only
   int page_size;
   int num_q_tiles;
-  int num_head_slots;  // CTAs' head dimension: hq / 2 with pairs, else hq
+  int num_head_slots;  // hq / 2 with pairs, else hq
+  // work plan (prefill_plan_kernel): plan[0] = q tiles in total, plan[1 + qt]
+  // = sequences with more than qt q tiles; those sequences sorted by q-tile
+  // count, most first: plan_seq[j] = {qs, q_len, ks, k_len}, plan_b[j] = b
+  // (null: direct enumeration of num_q_tiles x num_head_slots x num_seqs
+  // items, each checked against cu_seqlens)
+  const uint32_t* plan;
+  const uint4* plan_seq;
+  const uint32_t* plan_b;
   int num_seqs;
-  int num_items;       // num_q_tiles * num_head_slots * num_seqs
   int causal;
   float scale_log2;
   int* err;
@@ -331,17 +344,129 @@ __device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t p_tmem, ui
   }
 }
 
-// One work item = (q tile, head pair / head, sequence).  Items are numbered
-// q-tile-major with the heaviest causal tiles (last q tile) first, then head
-// slot, then sequence; round k hands gridDim.x consecutive items to the CTAs
-// (pf_work).  Returns 1 for an item with work, 0 for an empty one (q_len <= 1:
-// decode rows, or a tile past q_len), -1 for a sequence with k_len < q_len
-// (an error).
+// ---- work plan --------------------------------------------------------------
+// q tiles of sequence b (0: a decode row, q_len <= 1).  With `err`, records
+// k_len < q_len (then 0) and q_len > max_seqlen_q (clamped to num_q_tiles).
+__device__ __forceinline__ int pf_seq_tiles(const uint32_t* cu_q, const uint32_t* cu_k, int b,
+                                            int num_q_tiles, int* err) {
+  const int q_len = (int)(cu_q[b + 1] - cu_q[b]);
+  if (q_len <= 1) return 0;
+  if ((int)(cu_k[b + 1] - cu_k[b]) < q_len) {
+    if (err) record_error(err, NVKV_DEVERR_SEQLEN);
+    return 0;
+  }
+  const int n = (q_len + kPfBM - 1) / kPfBM;
+  if (n > num_q_tiles) {
+    if (err) record_error(err, NVKV_DEVERR_SEQLEN);
+    return num_q_tiles;
+  }
+  return n;
+}
+
+// Block-wide exclusive scan over 1024 threads; *total gets the sum.
+__device__ __forceinline__ uint32_t pf_block_excl_scan(uint32_t v, uint32_t* part,
+                                                       uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += t;
+  }
+  if (lane == 31) part[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t pv = part[lane];
+    uint32_t pi = pv;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, pi, d);
+      if (lane >= d) pi += t;
+    }
+    part[lane] = pi - pv;
+    if (lane == 31) *total = pi;
+  }
+  __syncthreads();
+  return part[warp] + incl - v;
+}
+
+// One CTA of 1024 threads: a counting sort of the prefill sequences by their
+// q-tile count (most first) into the plan, so the prefill kernel enumerates
+// exactly its work items, however many decode rows share the batch.  Within
+// one count the order follows the atomics; each item's arithmetic does not
+// depend on which CTA takes it, so outputs do not change with that order.
+// Plan layout: the counts, then (16-byte aligned) the records, then the ids.
+__host__ __device__ inline size_t pf_plan_seq_word(int num_q_tiles) {
+  return ((size_t)num_q_tiles + 1 + 3) & ~size_t(3);
+}
+
+__global__ void __launch_bounds__(1024)
+    prefill_plan_kernel(const uint32_t* cu_q, const uint32_t* cu_k, int num_seqs,
+                        int num_q_tiles, uint32_t* plan, int* err) {
+  pdl_launch_dependents();  // the prefill grid may start its prologue now
+  extern __shared__ uint32_t hist[];  // [num_q_tiles + 1]: sequences per count, then cursors
+  __shared__ uint32_t part[32], total, tiles;
+  const int tid = threadIdx.x, Q = num_q_tiles;
+  for (int i = tid; i <= Q; i += 1024) hist[i] = 0;
+  if (tid == 0) tiles = 0;
+  __syncthreads();
+  for (int b = tid; b < num_seqs; b += 1024) {
+    const int n = pf_seq_tiles(cu_q, cu_k, b, Q, err);
+    if (n > 0) {
+      atomicAdd(&hist[n], 1u);
+      atomicAdd(&tiles, (uint32_t)n);
+    }
+  }
+  __syncthreads();
+  // start[n] = sequences with more than n tiles: an exclusive scan over the
+  // counts in descending order (entry i of the scan is count Q - i), one
+  // contiguous chunk of it per thread
+  const int per = (Q + 1 + 1023) / 1024;
+  const int lo = tid * per, hi = min(lo + per, Q + 1);
+  uint32_t sum = 0;
+  for (int i = lo; i < hi; ++i) sum += hist[Q - i];
+  uint32_t run = pf_block_excl_scan(sum, part, &total);
+  for (int i = lo; i < hi; ++i) {
+    const int n = Q - i;
+    const uint32_t h = hist[n];
+    hist[n] = run;  // becomes the scatter cursor of count n
+    if (n < Q) plan[1 + n] = run;
+    run += h;
+  }
+  if (tid == 0) plan[0] = tiles;
+  __syncthreads();
+  uint4* seq = reinterpret_cast<uint4*>(plan + pf_plan_seq_word(Q));
+  uint32_t* ids = reinterpret_cast<uint32_t*>(seq + num_seqs);
+  for (int b = tid; b < num_seqs; b += 1024) {
+    const int n = pf_seq_tiles(cu_q, cu_k, b, Q, nullptr);
+    if (n > 0) {
+      const uint32_t pos = atomicAdd(&hist[n], 1u);
+      const uint32_t qs = cu_q[b], ks = cu_k[b];
+      seq[pos] = make_uint4(qs, cu_q[b + 1] - qs, ks, cu_k[b + 1] - ks);
+      ids[pos] = (uint32_t)b;
+    }
+  }
+}
+
+// One work item = (q tile, head pair / head, sequence).  Items run level by
+// level from the last q tile down (the heaviest causal tiles first); level qt
+// holds plan[1 + qt] sequences x num_head_slots, the head slot varying
+// fastest.  The level of item w is found by walking the (few, L1-resident)
+// level counts from the top on every call: nothing stays live across the
+// roles' tile loops, whose softmax warps are at the register limit.
 struct PfItem {
   int b, head0, kvh, i0, q_len, k_len, off, ntiles;
   uint32_t qs, ks;
 };
-__device__ __forceinline__ int pf_item(const PrefillParams& p, int w, PfItem& it) {
+template <bool kPlan>
+__device__ __forceinline__ int pf_num_items(const PrefillParams& p) {
+  return kPlan ? (int)__ldg(p.plan) * p.num_head_slots
+               : p.num_q_tiles * p.num_head_slots * p.num_seqs;
+}
+// Direct enumeration: the same level order with every sequence in each level;
+// returns false for an empty item (a decode row, a tile past q_len, or a bad
+// sequence, which is then reported).
+__device__ __forceinline__ bool pf_item_direct(const PrefillParams& p, int w, PfItem& it) {
   const int per_tile = p.num_head_slots * p.num_seqs;
   const int qt = p.num_q_tiles - 1 - w / per_tile;
   const int rem = w % per_tile;
@@ -352,15 +477,45 @@ __device__ __forceinline__ int pf_item(const PrefillParams& p, int w, PfItem& it
   it.qs = __ldg(p.cu_q + it.b);
   it.q_len = (int)(__ldg(p.cu_q + it.b + 1) - it.qs);
   it.i0 = qt * kPfBM;
-  if (it.q_len <= 1 || it.i0 >= it.q_len) return 0;  // q_len == 1 rows: decode kernel
+  if (it.q_len <= 1 || it.i0 >= it.q_len) return false;
   it.ks = __ldg(p.cu_k + it.b);
   it.k_len = (int)(__ldg(p.cu_k + it.b + 1) - it.ks);
   it.off = it.k_len - it.q_len;
-  if (it.off < 0) return -1;
+  if (it.off < 0 || (qt == p.num_q_tiles - 1 && it.q_len > p.num_q_tiles * kPfBM)) {
+    record_error(p.err, NVKV_DEVERR_SEQLEN);
+    if (it.off < 0) return false;
+  }
   const int last_row = min(it.i0 + kPfBM, it.q_len) - 1;
   const int kmax = p.causal ? min(it.k_len, last_row + it.off + 1) : it.k_len;
   it.ntiles = (kmax + kPfBN - 1) / kPfBN;
-  return 1;
+  return true;
+}
+template <bool kPlan>
+__device__ __forceinline__ bool pf_item(const PrefillParams& p, int w, PfItem& it) {
+  if (!kPlan) return pf_item_direct(p, w, it);
+  int qt = p.num_q_tiles - 1, base = 0;
+  for (; qt >= 0; --qt) {
+    const int n = (int)__ldg(p.plan + 1 + qt) * p.num_head_slots;
+    if (w < base + n) break;
+    base += n;
+  }
+  if (qt < 0) return false;
+  const int r = w - base;
+  const int y = r % p.num_head_slots, j = r / p.num_head_slots;
+  const uint4 e = __ldg(p.plan_seq + j);
+  it.b = (int)__ldg(p.plan_b + j);
+  it.head0 = p.pair ? 2 * y : y;
+  it.kvh = it.head0 / p.group;
+  it.qs = e.x;
+  it.q_len = (int)e.y;
+  it.i0 = qt * kPfBM;
+  it.ks = e.z;
+  it.k_len = (int)e.w;
+  it.off = it.k_len - it.q_len;
+  const int last_row = min(it.i0 + kPfBM, it.q_len) - 1;
+  const int kmax = p.causal ? min(it.k_len, last_row + it.off + 1) : it.k_len;
+  it.ntiles = (kmax + kPfBN - 1) / kPfBN;
+  return true;
 }
 
 // Item of round k for this CTA: rounds alternate direction (snake order), so
@@ -378,7 +533,7 @@ __device__ __forceinline__ int pf_work(int k) {
 // item i's last S MMA has read Q (q_empty).  O_x needs no extra barrier: its
 // next overwrite (item i+1's first PV, accumulate = 0) waits on p_full, which
 // the softmax warps arrive only after their epilogue has read O_x.
-template <typename T>
+template <typename T, bool kPlan>
 __global__ void __launch_bounds__(kPfThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q,
                          const __grid_constant__ CUtensorMap tmap_k,
@@ -421,6 +576,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the work plan (and the inputs) of the kernels before this one
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -430,13 +586,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma_prefetch_desc(&tmap_v);
       uint32_t nq = 0, t = 0;  // items loaded, K/V ring loads (running over items)
       bool ok = true;
-      for (int k = 0; ok && (int64_t)k * gridDim.x < p.num_items; ++k) {
+      for (int k = 0; ok && (int64_t)k * gridDim.x < pf_num_items<kPlan>(p); ++k) {
         const int w = pf_work(k);
-        if (w >= p.num_items) continue;
         PfItem it;
-        const int kind = pf_item(p, w, it);
-        if (kind < 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
-        if (kind <= 0) continue;
+        if (w >= pf_num_items<kPlan>(p) || !pf_item<kPlan>(p, w, it)) continue;
         if (nq > 0 && !mbar_wait(q_empty, (nq - 1) & 1u, p.err)) break;
         mbar_arrive_expect_tx(q_full, nslot * kPfTile);
         for (int x = 0; x < nslot; ++x) {
@@ -486,11 +639,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #define PF_FULL(t) (&kv_full[(t) % kPfSlots])
       uint32_t nq = 0, t = 0, g = 0;  // items, K/V ring position, key tiles per slot
       bool ok = true;
-      for (int k = 0; ok && (int64_t)k * gridDim.x < p.num_items; ++k) {
+      for (int k = 0; ok && (int64_t)k * gridDim.x < pf_num_items<kPlan>(p); ++k) {
         const int w = pf_work(k);
-        if (w >= p.num_items) continue;
         PfItem it;
-        if (pf_item(p, w, it) <= 0) continue;
+        if (w >= pf_num_items<kPlan>(p) || !pf_item<kPlan>(p, w, it)) continue;
         const int n = it.ntiles;
         // S_x(g) of the item's first key tile: Q and K_0 (S_x / P_x(g - 1) were
         // consumed by PV_x(g - 1), issued before it on the in-order pipe)
@@ -555,11 +707,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const uint32_t col_s = x ? 128u : 0u, col_o = x ? 384u : 256u;
       uint32_t g = 0;  // key tiles of this slot so far (running over items)
       bool alive = true;
-      for (int k = 0; alive && (int64_t)k * gridDim.x < p.num_items; ++k) {
+      for (int k = 0; alive && (int64_t)k * gridDim.x < pf_num_items<kPlan>(p); ++k) {
         const int w = pf_work(k);
-        if (w >= p.num_items) continue;
         PfItem it;
-        if (pf_item(p, w, it) <= 0) continue;
+        if (w >= pf_num_items<kPlan>(p) || !pf_item<kPlan>(p, w, it)) continue;
         const int qi = it.i0 + r;
         const int lim_row = p.causal ? min(it.k_len - 1, qi + it.off) : it.k_len - 1;
         float m_ref = -INFINITY, l = 0.f;
@@ -678,6 +829,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+size_t prefill_plan_bytes(int num_seqs, int max_seqlen_q) {
+  if (max_seqlen_q <= 1 || num_seqs <= 0) return 0;
+  const int q_tiles = (max_seqlen_q + kPfBM - 1) / kPfBM;
+  const size_t words = pf_plan_seq_word(q_tiles) + 5 * (size_t)num_seqs;
+  return (words * sizeof(uint32_t) + 255) & ~size_t(255);
+}
+
+template <typename T, bool kPlan>
+static int launch_prefill_grid(dim3 grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                               const CUtensorMap& mv, const PrefillParams& p,
+                               cudaStream_t stream) {
+  auto kern = paged_prefill_kernel<T, kPlan>;
+  static unsigned long long attr_done = 0;  // one per instantiation
+  int rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done);
+  if (rc) return rc;
+  return launch_pdl(kern, grid, dim3(kPfThreads), kPfSmemBytes, stream, "paged prefill launch",
+                    mq, mk, mv, p);
+}
+
 int launch_paged_prefill(const AttnArgs& a) {
   const int64_t rows = a.block_tables ? a.num_blocks * a.page : a.num_blocks;
   CUtensorMap mq, mk, mv;
@@ -701,31 +871,44 @@ int launch_paged_prefill(const AttnArgs& a) {
   p.page_size = a.page;
   p.num_q_tiles = (a.max_q + kPfBM - 1) / kPfBM;
   p.num_head_slots = p.pair ? a.hq / 2 : a.hq;
-  p.num_seqs = a.num_seqs;
-  const int64_t items = (int64_t)p.num_q_tiles * p.num_head_slots * a.num_seqs;
-  if (items > INT32_MAX - kPfCtas)
+  const int64_t items = (int64_t)p.num_q_tiles * p.num_head_slots * a.num_seqs;  // upper bound
+  if (items > INT32_MAX - kPfCtas || p.num_q_tiles > kPfMaxQTiles)
     return set_error(NVKV_ERR_UNSUPPORTED, "paged prefill: too many tiles");
   if (items == 0) return NVKV_OK;
-  p.num_items = (int)items;
+  const size_t plan_off =
+      attention_plan_offset(decode_workspace_bytes(a.num_seqs, a.hq, a.hkv, a.max_k));
+  const size_t plan_need = prefill_plan_bytes(a.num_seqs, a.max_q);
+  if (!a.ws || a.ws_bytes < plan_off + plan_need)
+    return set_error(NVKV_ERR_WORKSPACE, "paged prefill: workspace too small for the work plan");
+  // With few candidate items per CTA, walking them all costs less than the
+  // plan kernel in front of the grid; with many (decode rows sharing the
+  // batch) the plan removes the empty ones.
+  const bool use_plan = items > (int64_t)kPfCtas * kPfDirectItemsPerCta;
+  uint32_t* plan = use_plan ? reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a.ws) + plan_off)
+                            : nullptr;
+  p.plan = plan;
+  p.plan_seq = use_plan ? reinterpret_cast<const uint4*>(plan + pf_plan_seq_word(p.num_q_tiles))
+                        : nullptr;
+  p.plan_b = use_plan ? reinterpret_cast<const uint32_t*>(p.plan_seq + a.num_seqs) : nullptr;
+  p.num_seqs = a.num_seqs;
   p.causal = a.causal;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = device_error_word();
+  if (use_plan) {
+    prefill_plan_kernel<<<1, 1024, (p.num_q_tiles + 1) * sizeof(uint32_t), a.stream>>>(
+        a.cu_q, a.cu_k, a.num_seqs, p.num_q_tiles, plan, p.err);
+    rc = check_cuda(cudaGetLastError(), "prefill plan launch");
+    if (rc) return rc;
+  }
   // one persistent CTA per SM (the shared-memory footprint allows one)
   const dim3 grid((unsigned)std::min<int64_t>(items, kPfCtas));
-  if (a.dtype == NVKV_DTYPE_BF16) {
-    auto kern = paged_prefill_kernel<__nv_bfloat16>;
-    static unsigned long long attr_done_bf16 = 0;
-    rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done_bf16);
-    if (rc) return rc;
-    kern<<<grid, kPfThreads, kPfSmemBytes, a.stream>>>(mq, mk, mv, p);
-  } else {
-    auto kern = paged_prefill_kernel<__half>;
-    static unsigned long long attr_done_f16 = 0;
-    rc = ensure_smem_attr((const void*)kern, kPfSmemBytes, &attr_done_f16);
-    if (rc) return rc;
-    kern<<<grid, kPfThreads, kPfSmemBytes, a.stream>>>(mq, mk, mv, p);
-  }
-  return check_cuda(cudaGetLastError(), "paged prefill launch");
+  if (a.dtype == NVKV_DTYPE_BF16)
+    rc = use_plan ? launch_prefill_grid<__nv_bfloat16, true>(grid, mq, mk, mv, p, a.stream)
+                  : launch_prefill_grid<__nv_bfloat16, false>(grid, mq, mk, mv, p, a.stream);
+  else
+    rc = use_plan ? launch_prefill_grid<__half, true>(grid, mq, mk, mv, p, a.stream)
+                  : launch_prefill_grid<__half, false>(grid, mq, mk, mv, p, a.stream);
+  return rc;
 }
 
 }  // namespace nvkv

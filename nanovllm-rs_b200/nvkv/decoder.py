@@ -360,10 +360,11 @@ class Qwen3TP:
         """nvkv kernel launches one forward issues: per layer two RMSNorms
         (each fused with the all-reduce before it on the peer route), SiLU*mul,
         the prologue, the decode kernel, the combine kernel when the split-KV
-        plan splits, and the prefill kernel when any sequence has q_len > 1;
-        plus the final norm (on the peer route: the embedding's fused call,
-        the final norm being fused into the last layer's)."""
+        plan splits, and the prefill work plan + prefill kernel when
+        max_seqlen_q > 1; plus the final norm (on the peer route: the
+        embedding's fused call, the final norm being fused into the last
+        layer's)."""
         B = st.cu_seqlens_q.numel() - 1
-        split = ops.workspace_size(B, self.hq, self.hkv, st.max_seqlen_q, st.max_seqlen_k) > 0
-        per = 5 + (1 if split else 0) + (1 if st.max_seqlen_q > 1 else 0)
+        split = ops.workspace_size(B, self.hq, self.hkv, 1, st.max_seqlen_k) > 0
+        per = 5 + (1 if split else 0) + (2 if st.max_seqlen_q > 1 else 0)
         return per * self.cfg.num_hidden_layers + 1

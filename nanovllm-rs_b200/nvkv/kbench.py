@@ -14,6 +14,8 @@ Cases (one JSON line each; bytes/flops are the algorithmic figures):
   decode_32b_tp8  Qwen3-32B TP8 per GPU: B=64, 8q/1kv, L=32768            (HBM)
   prefill_8b      tcgen05 prefill, Qwen3-8B TP1: 16 prompts x 1024, causal (tensor)
   step_metadata   device-side decode-step metadata, 256 sequences (latency)
+  mixed_4b_tp1/2  config 3 (Qwen3-4B): 120 decodes + 8 fresh prompts in one
+                  call, with the decode-only and prefill-only parts     (mixed)
 Inputs of every HBM case exceed L2 or are rotated through enough copies
 that each timed launch reads cold data.
 """
@@ -173,6 +175,48 @@ def case_prefill(iters, nseq=16, L=1024, hq=32, hkv=8):
                 flops=4 * 128 * hq * pairs, s=med, bound="tensor")
 
 
+def case_mixed(iters, tp=1):
+    """BASELINE config 3 (Qwen3-4B, 32q/8kv, TP1/2): one continuous-batching
+    step of 120 decoding sequences (contexts U[129, 2304]) and 8 fresh
+    prompts U[128, 2048] in one nvkv_paged_attention call (decode kernel +
+    tcgen05 kernel), and each part alone for the split."""
+    page, hq, hkv = 256, 32 // tp, 8 // tp
+    rng = np.random.default_rng(9)
+    dec = rng.integers(129, 2305, 120)
+    pre = rng.integers(128, 2049, 8)
+    order = rng.permutation(128)
+    q_all = np.concatenate([np.ones(120, np.int64), pre])[order]
+    k_all = np.concatenate([dec, pre])[order]
+    nblk = int(sum((int(L) + page - 1) // page for L in k_all)) + 2
+    caches, bt_all = _paged(k_all, page, hkv, nblk, 11)
+    kc, vc = caches[0]
+
+    def setup(qs, ks, sel):
+        T = int(qs.sum())
+        q = torch.randn(T, hq, 128, device="cuda").bfloat16()
+        cuq = torch.from_numpy(np.concatenate([[0], np.cumsum(qs)]).astype(np.int32)).cuda()
+        cuk = torch.from_numpy(np.concatenate([[0], np.cumsum(ks)]).astype(np.int32)).cuda()
+        bt = bt_all[torch.from_numpy(sel).cuda()].contiguous()
+        mq, mk = int(qs.max()), int(ks.max())
+        ws = torch.empty(max(16, ops.workspace_size(len(qs), hq, hkv, mq, mk)), dtype=torch.uint8,
+                         device="cuda")
+        out = torch.empty_like(q)
+        return lambda i: ops.paged_attention(q, kc, vc, cuq, cuk, bt, mq, mk, 128 ** -0.5,  # noqa
+                                             out=out, workspace=ws)
+
+    idx = np.arange(128)
+    t_mix, _ = _time(setup(q_all, k_all, idx), iters)
+    d = q_all == 1
+    t_dec, _ = _time(setup(q_all[d], k_all[d], idx[d]), iters)
+    t_pre, _ = _time(setup(q_all[~d], k_all[~d], idx[~d]), iters)
+    dbytes = int(k_all[d].sum()) * hkv * 128 * 2 * 2 + 2 * int(d.sum()) * hq * 128 * 2
+    pairs = int(sum(int(L) * (int(L) + 1) // 2 for L in k_all[~d]))
+    return dict(kernel="mixed_step", tp=tp, hq=hq, hkv=hkv, decode_seqs=int(d.sum()),
+                prefill_tokens=int(q_all[~d].sum()), bytes=dbytes, flops=4 * 128 * hq * pairs,
+                s=t_mix, decode_only_us=round(t_dec * 1e6, 2), prefill_only_us=round(t_pre * 1e6, 2),
+                bound="mixed")
+
+
 CASES = {
     "store_cfg2": lambda it: case_store(72, 8, it),
     "store_prefill": lambda it: case_store(16384, 0, it),
@@ -192,6 +236,8 @@ CASES = {
         "decode_32b_tp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
     "prefill_8b": lambda it: case_prefill(it),
     "step_metadata": lambda it: case_step_metadata(256, it),
+    "mixed_4b_tp1": lambda it: case_mixed(it, 1),
+    "mixed_4b_tp2": lambda it: case_mixed(it, 2),
 }
 
 
@@ -205,6 +251,14 @@ def main(argv=None):
         r = CASES[name](a.iters)
         if r["bound"] == "latency":  # a few KB: only the time means anything
             r.update(case=name, us=round(r["s"] * 1e6, 2))
+        elif r["bound"] == "mixed":  # each part against its own roofline, timed alone
+            gbs = r["bytes"] / (r["decode_only_us"] * 1e-6) / 1e9
+            tfs = r["flops"] / (r["prefill_only_us"] * 1e-6) / 1e12
+            r.update(case=name, us=round(r["s"] * 1e6, 2),
+                     decode_gbs=round(gbs, 1), decode_frac=round(gbs / hbm, 4),
+                     prefill_tflops=round(tfs, 1), prefill_frac=round(tfs / tf, 4),
+                     parts_sum_over_mixed=round((r["decode_only_us"] + r["prefill_only_us"])
+                                                / (r["s"] * 1e6), 3), peak_source=src)
         elif r["bound"] == "hbm":
             ach = r["bytes"] / r["s"] / 1e9
             r.update(case=name, us=round(r["s"] * 1e6, 2), achieved_gbs=round(ach, 1),

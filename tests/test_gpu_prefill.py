@@ -94,3 +94,77 @@ def test_mixed_decode_and_prefill_batch():
 
 def test_prefill_page_128():
     _paged_case([200, 5], [600, 133], 4, 1, page=128, seed=6)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_config3_mixed_step_qwen3_4b(tp):
+    """BASELINE config 3 (Qwen3-4B, 32 q / 8 kv heads, TP1/2): a continuous-
+    batching step with decoding sequences (contexts U[129, 2304]) next to
+    fresh prompts and a prefix-cache-hit chunk, at the per-rank head counts."""
+    rng = np.random.default_rng(30 + tp)
+    dec = rng.integers(129, 2305, 24).tolist()
+    q_lens = [1] * len(dec) + [700, 1300, 150]
+    k_lens = dec + [700, 1300, 150 + 512]
+    order = rng.permutation(len(q_lens))  # decode and prefill rows interleaved
+    _paged_case([q_lens[i] for i in order], [k_lens[i] for i in order], 32 // tp, 8 // tp,
+                seed=40 + tp)
+
+
+def test_prefill_bad_lengths_reported():
+    """The prefill work plan checks each q_len > 1 sequence: k_len < q_len, or
+    q_len above max_seqlen_q (whose tail rows the kernel cannot cover), is
+    reported as DEVERR_SEQLEN; the other sequences are still computed."""
+    g = torch.Generator().manual_seed(21)
+    d, hq, hkv = 128, 4, 2
+    for q_lens, k_lens, max_q in (([300, 40], [300, 30], 300),   # k_len < q_len
+                                  ([300, 40], [300, 40], 200)):  # q_len > max_seqlen_q
+        T, Tk = sum(q_lens), sum(k_lens)
+        q = torch.randn(T, hq, d, generator=g).bfloat16().cuda()
+        k = torch.randn(Tk, hkv, d, generator=g).bfloat16().cuda()
+        v = torch.randn(Tk, hkv, d, generator=g).bfloat16().cuda()
+        nvkv.device_error()
+        out = nvkv.paged_attention(q, k, v, cu(q_lens), cu(k_lens), None, max_q, max(k_lens),
+                                   d ** -0.5)
+        torch.cuda.synchronize()
+        assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
+        good = 0 if k_lens[0] == q_lens[0] and q_lens[0] <= max_q else 1
+        c, ck = np.cumsum([0] + q_lens), np.cumsum([0] + k_lens)
+        want = O.causal_attention_one(f32(q)[c[good]:c[good + 1]], f32(k)[ck[good]:ck[good + 1]],
+                                      f32(v)[ck[good]:ck[good + 1]], d ** -0.5, True)
+        assert_attention_close(out[c[good]:c[good + 1]], want, "the well-formed sequence")
+
+
+def test_mixed_many_decode_rows_work_plan():
+    """Hundreds of decode rows next to two prompts: the candidate work items
+    (q tiles x head slots x sequences) exceed the direct-enumeration limit,
+    so the prefill kernel runs from its work plan (prompts sorted by q-tile
+    count); every row, decode and prefill, matches the oracle."""
+    rng = np.random.default_rng(50)
+    dec = rng.integers(2, 700, 300).tolist()
+    q_lens = [1] * 300 + [200, 517]
+    k_lens = dec + [200, 517 + 300]
+    order = rng.permutation(len(q_lens))
+    _paged_case([q_lens[i] for i in order], [k_lens[i] for i in order], 8, 2, seed=51)
+
+
+def test_work_plan_bad_lengths_reported():
+    """The work plan's own checks (k_len < q_len; q_len above max_seqlen_q)
+    with enough decode rows that the plan is used."""
+    g = torch.Generator().manual_seed(52)
+    d, hq, hkv = 128, 8, 2
+    for q_pre, k_pre, max_q in (([300, 40], [300, 30], 300), ([300, 40], [300, 40], 200)):
+        q_lens, k_lens = [1] * 400 + q_pre, [5] * 400 + k_pre
+        T, Tk = sum(q_lens), sum(k_lens)
+        q = torch.randn(T, hq, d, generator=g).bfloat16().cuda()
+        k = torch.randn(Tk, hkv, d, generator=g).bfloat16().cuda()
+        v = torch.randn(Tk, hkv, d, generator=g).bfloat16().cuda()
+        nvkv.device_error()
+        out = nvkv.paged_attention(q, k, v, cu(q_lens), cu(k_lens), None, max_q, max(k_lens),
+                                   d ** -0.5)
+        torch.cuda.synchronize()
+        assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
+        good = 400 + (0 if k_pre[0] == q_pre[0] and q_pre[0] <= max_q else 1)
+        c, ck = np.cumsum([0] + q_lens), np.cumsum([0] + k_lens)
+        want = O.causal_attention_one(f32(q)[c[good]:c[good + 1]], f32(k)[ck[good]:ck[good + 1]],
+                                      f32(v)[ck[good]:ck[good + 1]], d ** -0.5, True)
+        assert_attention_close(out[c[good]:c[good + 1]], want, "the well-formed prompt")
