@@ -60,12 +60,15 @@ constexpr int kPfNumBars = 2 + 2 * kPfSlots + 6;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfCtas = 148;  // B200 SMs
-// Candidate items per CTA up to which the kernel enumerates every (q tile,
-// head slot, sequence) instead of building a work plan first (measured on the
-// 8B prefill, 16 x 1024: 197 us direct against 212 us with the plan; a mixed
-// step of 120 decodes + 8 prompts, 221 candidates per CTA: 362 us direct
-// against 265 us with the plan).
-constexpr int kPfDirectItemsPerCta = 32;
+// Direct enumeration of every candidate (q tile, head slot, sequence) is kept
+// when nearly all candidates are real work (the query tokens fill at least
+// kPfDirectFill of the candidate q tiles: uniform prompts) or the batch is
+// tiny (at most kPfDirectItemsPerCta candidates per CTA); otherwise the work
+// plan goes first.  Measured: 16 x 1024 prompts, direct 196.5 us / plan
+// 211.6 us; 8 prompts U[128, 2048], direct 181.9 / plan 156.5; 120 decodes +
+// those 8 prompts, direct 362 / plan 267.
+constexpr int kPfDirectItemsPerCta = 2;
+constexpr double kPfDirectFill = 0.9;
 constexpr float kPfRescaleLog2 = 8.0f;
 // One exponential pair in NVKV_PF_POLY_EVERY runs on the FMA-pipe polynomial
 // instead of MUFU ex2 (0: all on MUFU), balancing the two pipes.  Measured on
@@ -880,10 +883,12 @@ int launch_paged_prefill(const AttnArgs& a) {
   const size_t plan_need = prefill_plan_bytes(a.num_seqs, a.max_q);
   if (!a.ws || a.ws_bytes < plan_off + plan_need)
     return set_error(NVKV_ERR_WORKSPACE, "paged prefill: workspace too small for the work plan");
-  // With few candidate items per CTA, walking them all costs less than the
-  // plan kernel in front of the grid; with many (decode rows sharing the
-  // batch) the plan removes the empty ones.
-  const bool use_plan = items > (int64_t)kPfCtas * kPfDirectItemsPerCta;
+  // Empty candidates (decode rows, tiles past a short prompt) cost a skip and
+  // leave holes in the balanced rounds; the plan removes them but costs a
+  // launch in front of the grid.
+  const int64_t cand_tiles = (int64_t)p.num_q_tiles * a.num_seqs;
+  const bool use_plan = items > (int64_t)kPfCtas * kPfDirectItemsPerCta &&
+                        (double)(a.num_q_rows / kPfBM) < kPfDirectFill * (double)cand_tiles;
   uint32_t* plan = use_plan ? reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a.ws) + plan_off)
                             : nullptr;
   p.plan = plan;
