@@ -87,6 +87,26 @@ def test_workspace_zero_when_no_split():
     assert need.value == 0
 
 
+def test_workspace_holds_prefill_plan():
+    """A call that may prefill (max_seqlen_q > 1) needs room for the prefill
+    work plan even when the decode plan does not split; the plan grows with
+    the batch (a record per sequence) and with max_seqlen_q (a count per
+    128-row q tile), and the decode scratch sits in front of it."""
+    from nvkv._lib import lib
+    def size(B, max_q, max_k, hq=32, hkv=8):
+        need = ctypes.c_size_t(0)
+        assert lib.nvkv_paged_attention_workspace_size(B, hq, hkv, 128, max_q, max_k,
+                                                       ctypes.byref(need)) == 0
+        return need.value
+    assert size(256, 1, 1536) == 0
+    assert size(256, 2, 1536) > 0
+    assert size(4096, 1024, 1536) > size(256, 1024, 1536) >= 256 * 20
+    assert size(256, 1 << 20, 1536) - size(256, 1024, 1536) >= 4 * ((1 << 20) - 1024) // 128
+    for B, max_k in ((64, 4096), (8, 32768)):  # decode splits: scratch + plan
+        dec = size(B, 1, max_k)
+        assert dec > 0 and size(B, 512, max_k) >= dec + B * 20
+
+
 def test_context_and_attention_objects_host_only():
     from nvkv._lib import lib, ERR_INVALID_ARG, OK
     assert lib.nvkv_context_set(None, None, 1, 1, 1, None, 0, None, None, 0) == ERR_INVALID_ARG
