@@ -1,5 +1,6 @@
 // Host-side status plumbing, the per-device error word and tensor-map
 // encoding shared by every nvkv entry point.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -18,7 +19,9 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 int* g_err_ptr[kMaxDevices] = {nullptr};
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+// Looked up once; published with release/acquire so callers on other threads
+// see a complete pointer without taking the lock.
+std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode{nullptr};
 }  // namespace
 
 int set_error(int code, const std::string& msg) {
@@ -59,34 +62,38 @@ int ensure_smem_attr(const void* kernel, int bytes, unsigned long long* done) {
   return NVKV_OK;
 }
 
-static int get_encoder() {
-  if (g_encode) return NVKV_OK;
+static int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  *out = g_encode.load(std::memory_order_acquire);
+  if (*out) return NVKV_OK;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_encode) return NVKV_OK;
+  *out = g_encode.load(std::memory_order_relaxed);
+  if (*out) return NVKV_OK;
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult q;
   cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
                                                    cudaEnableDefault, &q);
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
     return set_error(NVKV_ERR_CUDA, "cuTensorMapEncodeTiled entry point not available");
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  *out = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  g_encode.store(*out, std::memory_order_release);
   return NVKV_OK;
 }
 
 int encode_kv_tensor_map(CUtensorMap* map, const void* base, int64_t head_dim, int64_t num_heads,
                          int64_t num_rows, int64_t row_stride_bytes, int box_inner, int box_rows,
                          bool swizzle128) {
-  int rc = get_encoder();
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  int rc = get_encoder(&encode);
   if (rc) return rc;
   // dim0 = head_dim (contiguous), dim1 = heads, dim2 = rows (tokens / slots)
   cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_heads, (cuuint64_t)num_rows};
   cuuint64_t strides[2] = {(cuuint64_t)(head_dim * 2), (cuuint64_t)row_stride_bytes};
   cuuint32_t box[3] = {(cuuint32_t)box_inner, 1u, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1u, 1u, 1u};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(NVKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " +
                                         std::to_string((int)r) + ")");
