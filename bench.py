@@ -433,6 +433,7 @@ def run_nvkv(a):
         if world == 1:
             line["cpu_baseline"] = cpu_reference(max_seconds=20.0)
             line["op_level"] = op_level_config2()
+            line["block_manager"] = block_manager_host()
         print(json.dumps(line), flush=True)
     # a graph holding NCCL calls must be released before the process group
     run = None
@@ -520,6 +521,67 @@ def _all_host_threads():
     except Exception:
         pass
     return n
+
+
+def block_manager_host(B=256, prompt=1024, shared=512, page=256, steps=64):
+    """The KV block manager on the host (config 4's shape: 256 sequences x
+    1024-token prompts, P=256, half sharing a 512-token prefix): admission
+    (get_token_layout, can_allocate, allocate) and `steps` decode steps
+    (can_append, may_append) through the C ABI, next to the Python
+    restatement of the reference's manager (oracle, one thread) on the same
+    workload.  Host clock; the reference's own manager is compiled Rust, so
+    the port's time is a baseline, not the reference's speed."""
+    try:
+        from nvkv import kbench
+        c = kbench.case_block_manager(1, B=B, prompt=prompt, shared=shared, page=page, steps=steps)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import block_manager_oracle as OB
+        rng = np.random.default_rng(12)
+        pre = [int(t) for t in rng.integers(0, 151936, shared)]
+        nb = B * ((prompt + steps + page - 1) // page) + 8
+        bm = OB.BlockManager(nb, page)
+        seqs = []
+        for b in range(B):
+            toks = [int(t) for t in rng.integers(0, 151936, prompt)]
+            if b % 2 == 0:
+                toks[:shared] = pre
+            seqs.append(OB.Seq(toks, page))
+        t0 = time.perf_counter()
+        for s in seqs:
+            _, free, new = bm.get_token_layout(s)
+            bm.can_allocate(free + new)
+            s.num_new_tokens = new
+            bm.allocate(s)
+            s.num_cached_tokens += s.num_new_tokens
+            s.num_new_tokens = 0
+        t1 = time.perf_counter()
+        for _ in range(steps):
+            for s in seqs:
+                s.append_token(7)
+                bm.can_append(s, 1)
+                s.num_new_tokens = 1
+                bm.may_append(s)
+                s.num_cached_tokens += 1
+                s.num_new_tokens = 0
+        t2 = time.perf_counter()
+        port = {"admission_us_per_seq": round((t1 - t0) / B * 1e6, 2),
+                "decode_step_us": round((t2 - t1) / steps * 1e6, 1), "cores": 1,
+                "kind": "port", "sample": "the same workload, Python restatement "
+                                          "(oracle/block_manager_oracle.py)"}
+        return {"workload": f"{B} seqs x {prompt}-token prompts, P={page}, half sharing a "
+                            f"{shared}-token prefix; admission + {steps} decode steps",
+                "nvkv": {"admission_us_per_seq": c["admission_us_per_seq"],
+                         "decode_step_us": c["decode_step_us"],
+                         "decode_step_batched_us": c["decode_step_batched_us"],
+                         "note": "C ABI via ctypes (~1 us per call included); batched = "
+                                 "nvkv_block_manager_append_batch, one call per step"},
+                "cpu_port": port,
+                "admission_speedup_vs_port": round(port["admission_us_per_seq"]
+                                                   / c["admission_us_per_seq"], 1),
+                "decode_step_speedup_vs_port": round(port["decode_step_us"]
+                                                     / c["decode_step_batched_us"], 1)}
+    except Exception as e:  # a side measurement never breaks the bench line
+        return {"error": f"{type(e).__name__}: {e}"}
 
 
 def op_level_config2(seed=2, reps=20):

@@ -333,6 +333,78 @@ int nvkv_attention_forward(nvkv_attention_t attn, const void* q, int64_t q_strid
                            int64_t num_tokens, int num_q_heads, int num_kv_heads, void* out,
                            int dtype, nvkv_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * KV-pool block manager with prefix caching: BlockManager
+ * (engine/block_manager.rs:35-287), host-only.  It hands out the page ids
+ * that block_tables and slot_mapping are built from, with the reference's
+ * choices (same ids, same order, same hash chain), so prefix-cache hits
+ * share pages exactly as the reference's engine would.  Full blocks are
+ * keyed by xxh64 (seed 0) over the previous block's hash (omitted when -1)
+ * and the block's token ids, each a little-endian i64 (compute_hash,
+ * :53-64; xxhash-rust 0.8.16).  Where the reference asserts (a non-empty
+ * block table on allocate or get_token_layout, a hashed block under
+ * may_append, a ref count below zero) or would run out of free blocks, the
+ * call returns NVKV_ERR_INVALID_ARG and changes nothing.  One caller at a
+ * time per manager.
+ * ---------------------------------------------------------------------- */
+typedef struct nvkv_block_manager* nvkv_block_manager_t;
+
+/* The block-manager view of a Sequence (engine/sequence.rs:20-60).  The
+ * caller owns both arrays; the calls update the counters and the table. */
+typedef struct nvkv_block_seq {
+  const uint32_t* token_ids;    /* all tokens so far (prompt + completion)  */
+  int64_t num_tokens;
+  int64_t num_cached_tokens;    /* Sequence::num_cached_tokens (in/out)     */
+  int64_t num_new_tokens;       /* Sequence::num_new_tokens (in; the
+                                   scheduler sets it; deallocate zeroes it) */
+  uint32_t* block_table;        /* Sequence::block_table (in/out)           */
+  int64_t block_table_len;      /* entries in use (in/out)                  */
+  int64_t block_table_capacity; /* entries block_table can hold             */
+} nvkv_block_seq;
+
+/* BlockManager::compute_hash(token_ids, prefix) (:53-64); prefix -1 = none. */
+int nvkv_block_hash(const int64_t* token_ids, int64_t num_tokens, int64_t prefix,
+                    int64_t* hash_out);
+/* BlockManager::new(num_blocks, block_size) (:44-52): all blocks free, in id order. */
+int nvkv_block_manager_create(int64_t num_blocks, int64_t block_size,
+                              nvkv_block_manager_t* out);
+int nvkv_block_manager_destroy(nvkv_block_manager_t bm);
+/* free_block_ids.len() */
+int nvkv_block_manager_num_free(nvkv_block_manager_t bm, int64_t* out);
+/* can_allocate(num_tokens) (:93-96) */
+int nvkv_block_manager_can_allocate(nvkv_block_manager_t bm, int64_t num_tokens, int* out);
+/* get_token_layout(seq) (:99-134): (tokens cached in used blocks, cached in
+ * free blocks, new) for a waiting sequence. */
+int nvkv_block_manager_get_token_layout(nvkv_block_manager_t bm, const nvkv_block_seq* seq,
+                                        int64_t* in_used, int64_t* in_free, int64_t* fresh);
+/* allocate(seq) (:136-190): prefix-cache hits, then fresh blocks for
+ * num_new_tokens; advances num_cached_tokens by the hits. */
+int nvkv_block_manager_allocate(nvkv_block_manager_t bm, nvkv_block_seq* seq);
+/* deallocate(seq) (:193-204) */
+int nvkv_block_manager_deallocate(nvkv_block_manager_t bm, nvkv_block_seq* seq);
+/* can_append(seq, num_new_tokens) (:207-220) */
+int nvkv_block_manager_can_append(nvkv_block_manager_t bm, const nvkv_block_seq* seq,
+                                  int64_t num_new_tokens, int* out);
+/* may_append(seq) (:222-284): blocks (and hashes of blocks that fill up)
+ * for the num_new_tokens after num_cached_tokens of a running sequence. */
+int nvkv_block_manager_may_append(nvkv_block_manager_t bm, nvkv_block_seq* seq);
+/* The scheduler's running-queue pass (scheduler.rs:103-140) in one call: in
+ * order, can_append(seqs[i], num_new_tokens[i]) then (if it fits) set
+ * num_new_tokens and may_append.  Stops at the first sequence that does not
+ * fit, with *done = its index, so the caller preempts from the back as the
+ * reference does and calls again from there (*done = n: all fit). */
+int nvkv_block_manager_append_batch(nvkv_block_manager_t bm, nvkv_block_seq* seqs, int64_t n,
+                                    const int64_t* num_new_tokens, int64_t* done);
+/* Introspection (no reference counterpart): one block's ref count, hash,
+ * stored token count and used flag; the free list front to back (*count is
+ * its full length, ids gets the first `capacity`); the hash map lookup. */
+int nvkv_block_manager_block_info(nvkv_block_manager_t bm, int64_t block_id,
+                                  int64_t* ref_count, int64_t* hash, int64_t* num_token_ids,
+                                  int* used);
+int nvkv_block_manager_free_ids(nvkv_block_manager_t bm, uint32_t* ids, int64_t capacity,
+                                int64_t* count);
+int nvkv_block_manager_lookup(nvkv_block_manager_t bm, int64_t hash, int64_t* block_id);
+
 #ifdef __cplusplus
 }
 #endif

@@ -104,7 +104,10 @@ int encode_kv_tensor_map(CUtensorMap* map, const void* base, int64_t head_dim, i
 
 extern "C" {
 
-int nvkv_version(void) { return 100; }
+int nvkv_version(void) {
+  nvkv::clear_error();
+  return 100;
+}
 
 const char* nvkv_last_error(void) { return nvkv::g_last_error.c_str(); }
 

@@ -42,6 +42,20 @@ _i32 = ctypes.c_int
 _f32 = ctypes.c_float
 _sz = ctypes.c_size_t
 
+
+
+class BlockSeq(ctypes.Structure):
+    """nvkv_block_seq: the block manager's view of a Sequence."""
+    _fields_ = [("token_ids", ctypes.c_void_p), ("num_tokens", ctypes.c_int64),
+                ("num_cached_tokens", ctypes.c_int64), ("num_new_tokens", ctypes.c_int64),
+                ("block_table", ctypes.c_void_p), ("block_table_len", ctypes.c_int64),
+                ("block_table_capacity", ctypes.c_int64)]
+
+
+_seq = ctypes.POINTER(BlockSeq)
+_pi64 = ctypes.POINTER(ctypes.c_int64)
+_pi32 = ctypes.POINTER(ctypes.c_int)
+
 # name -> argtypes, in the order of include/nvkv.h
 SIGNATURES = {
     "nvkv_version": [],
@@ -72,6 +86,20 @@ SIGNATURES = {
     "nvkv_attention_destroy": [_p],
     "nvkv_attention_set_kv_cache": [_p, _p, _p, _i64, _i32, _i32, _i32, _i32],
     "nvkv_attention_forward": [_p, _p, _i64, _p, _i64, _p, _i64, _i64, _i32, _i32, _p, _i32, _p],
+    "nvkv_block_hash": [_p, _i64, _i64, _pi64],
+    "nvkv_block_manager_create": [_i64, _i64, ctypes.POINTER(_p)],
+    "nvkv_block_manager_destroy": [_p],
+    "nvkv_block_manager_num_free": [_p, _pi64],
+    "nvkv_block_manager_can_allocate": [_p, _i64, _pi32],
+    "nvkv_block_manager_get_token_layout": [_p, _seq, _pi64, _pi64, _pi64],
+    "nvkv_block_manager_allocate": [_p, _seq],
+    "nvkv_block_manager_deallocate": [_p, _seq],
+    "nvkv_block_manager_can_append": [_p, _seq, _i64, _pi32],
+    "nvkv_block_manager_may_append": [_p, _seq],
+    "nvkv_block_manager_append_batch": [_p, _seq, _i64, _p, _pi64],
+    "nvkv_block_manager_block_info": [_p, _i64, _pi64, _pi64, _pi64, _pi32],
+    "nvkv_block_manager_free_ids": [_p, _p, _i64, _pi64],
+    "nvkv_block_manager_lookup": [_p, _i64, _pi64],
 }
 
 
