@@ -579,9 +579,34 @@ def block_manager_host(B=256, prompt=1024, shared=512, page=256, steps=64):
                 "admission_speedup_vs_port": round(port["admission_us_per_seq"]
                                                    / c["admission_us_per_seq"], 1),
                 "decode_step_speedup_vs_port": round(port["decode_step_us"]
-                                                     / c["decode_step_batched_us"], 1)}
+                                                     / c["decode_step_batched_us"], 1),
+                "prepare_step": _prepare_step_host()}
     except Exception as e:  # a side measurement never breaks the bench line
         return {"error": f"{type(e).__name__}: {e}"}
+
+
+def _prepare_step_host():
+    """prepare_model_input on the host: nvkv_prepare_step (C ABI) against the
+    oracle's restatement, on config 4's decode step and a 16 x 1024 prefill."""
+    from nvkv import kbench
+    import nvkv_oracle as O
+    c = kbench.case_step_prepare(1)
+    port = {}
+    for kind in ("decode", "prefill"):
+        arr, keep, pairs, ctx, new = kbench.step_prepare_inputs(kind)
+        seqs = [O.Seq([int(t) for t in toks], [int(b) for b in table], int(L - n), int(n), 256)
+                for (toks, table), L, n in zip(pairs, ctx, new)]
+        reps = 5
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            O.prepare_model_input(seqs, 256)
+        port[kind + "_us"] = round((time.perf_counter() - t0) / reps * 1e6, 1)
+    return {"nvkv": {k: c[k] for k in ("decode_us", "prefill_us", "decode_tokens",
+                                       "prefill_tokens")},
+            "cpu_port": dict(port, cores=1, kind="port",
+                             sample="oracle prepare_model_input, same steps"),
+            "decode_speedup_vs_port": round(port["decode_us"] / c["decode_us"], 1),
+            "prefill_speedup_vs_port": round(port["prefill_us"] / c["prefill_us"], 1)}
 
 
 def op_level_config2(seed=2, reps=20):

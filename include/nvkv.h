@@ -405,6 +405,40 @@ int nvkv_block_manager_free_ids(nvkv_block_manager_t bm, uint32_t* ids, int64_t 
                                 int64_t* count);
 int nvkv_block_manager_lookup(nvkv_block_manager_t bm, int64_t hash, int64_t* block_id);
 
+/* ------------------------------------------------------------------------
+ * Host-side step metadata: ModelRunner::prepare_model_input and
+ * prepare_block_tables (engine/model_runner.rs:53-160) for any step, from
+ * the block manager's sequence views, into caller-owned (e.g. pinned host)
+ * buffers.  For each sequence: input ids and positions of its
+ * num_new_tokens after num_cached_tokens, cu_seqlens_q/k (+= num_new /
+ * num_context tokens), context_lens, slot_mapping for the blocks from
+ * num_cached_tokens / block_size on, seq_need_compute_logits (indices of
+ * sequences whose context covers all their tokens and that have blocks);
+ * block_tables [num_seqs, width] padded with 0 only when sum(k) > sum(q).
+ * The reference's warm-up rule holds: a sequence without blocks gets no
+ * slots.  *sizes is always filled; with every output pointer NULL the call
+ * is a size query and returns NVKV_OK, so a caller sizes its buffers with
+ * one call and fills them with a second.  Outputs:
+ * input_ids/positions [num_tokens], cu_seqlens_q/k [num_seqs + 1],
+ * context_lens [num_seqs], need_logits [num_need_logits], slot_mapping
+ * [num_slots], block_tables [num_seqs * block_table_width].  Bit-exact.
+ * ---------------------------------------------------------------------- */
+typedef struct nvkv_step_sizes {
+  int64_t num_tokens;         /* input_ids / positions entries           */
+  int64_t num_slots;          /* slot_mapping entries                    */
+  int64_t num_need_logits;    /* seq_need_compute_logits entries         */
+  int64_t block_table_width;  /* max block-table length                  */
+  int64_t max_seqlen_q;
+  int64_t max_seqlen_k;
+  int has_block_tables;       /* 1 when sum(context) > sum(new tokens)   */
+} nvkv_step_sizes;
+
+int nvkv_prepare_step(const nvkv_block_seq* seqs, int64_t num_seqs, int64_t block_size,
+                      int64_t* input_ids, int64_t* positions, uint32_t* cu_seqlens_q,
+                      uint32_t* cu_seqlens_k, int64_t* slot_mapping, int64_t* context_lens,
+                      int64_t* need_logits, uint32_t* block_tables, int64_t capacity_tokens,
+                      int64_t capacity_slots, int64_t capacity_table, nvkv_step_sizes* sizes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,14 @@ class BlockSeq(ctypes.Structure):
                 ("block_table_capacity", ctypes.c_int64)]
 
 
+class StepSizes(ctypes.Structure):
+    """nvkv_step_sizes: the output sizes of nvkv_prepare_step."""
+    _fields_ = [("num_tokens", ctypes.c_int64), ("num_slots", ctypes.c_int64),
+                ("num_need_logits", ctypes.c_int64), ("block_table_width", ctypes.c_int64),
+                ("max_seqlen_q", ctypes.c_int64), ("max_seqlen_k", ctypes.c_int64),
+                ("has_block_tables", ctypes.c_int)]
+
+
 _seq = ctypes.POINTER(BlockSeq)
 _pi64 = ctypes.POINTER(ctypes.c_int64)
 _pi32 = ctypes.POINTER(ctypes.c_int)
@@ -100,6 +108,8 @@ SIGNATURES = {
     "nvkv_block_manager_block_info": [_p, _i64, _pi64, _pi64, _pi64, _pi32],
     "nvkv_block_manager_free_ids": [_p, _p, _i64, _pi64],
     "nvkv_block_manager_lookup": [_p, _i64, _pi64],
+    "nvkv_prepare_step": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                          ctypes.POINTER(StepSizes)],
 }
 
 

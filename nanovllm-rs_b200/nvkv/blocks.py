@@ -15,7 +15,7 @@ from typing import List, Sequence as Seq_, Tuple
 
 import numpy as np
 
-from ._lib import BlockSeq, check, lib
+from ._lib import BlockSeq, StepSizes, check, lib
 
 
 class Sequence:
@@ -179,3 +179,38 @@ class BlockManager:
         out = ctypes.c_int64(0)
         check(lib.nvkv_block_manager_lookup(self._h, int(h), ctypes.byref(out)))
         return int(out.value)
+
+
+def prepare_step(seqs, block_size: int) -> dict:
+    """ModelRunner::prepare_model_input + prepare_block_tables
+    (engine/model_runner.rs:53-160) for a list of Sequences: input_ids,
+    positions and the Context fields (cu_seqlens_q/k, max_seqlen_q/k,
+    slot_mapping, context_lens, block_tables or None, seq_need_compute_logits),
+    as numpy arrays of the reference's dtypes."""
+    ms = [_Marshal(s) for s in seqs]
+    arr = (BlockSeq * max(len(ms), 1))(*[m.c for m in ms])
+    sizes = StepSizes()
+    check(lib.nvkv_prepare_step(arr, len(ms), block_size, None, None, None, None, None, None,
+                                None, None, 0, 0, 0, ctypes.byref(sizes)))  # size query
+    B = len(ms)
+    w = int(sizes.block_table_width) if sizes.has_block_tables else 0
+    out = dict(input_ids=np.zeros(sizes.num_tokens, np.int64),
+               positions=np.zeros(sizes.num_tokens, np.int64),
+               cu_seqlens_q=np.zeros(B + 1, np.uint32), cu_seqlens_k=np.zeros(B + 1, np.uint32),
+               slot_mapping=np.zeros(sizes.num_slots, np.int64),
+               context_lens=np.zeros(B, np.int64),
+               seq_need_compute_logits=np.zeros(sizes.num_need_logits, np.int64),
+               block_tables=np.zeros((B, w), np.uint32) if sizes.has_block_tables else None)
+
+    def ptr(a):
+        return a.ctypes.data if a is not None and a.size else None
+
+    check(lib.nvkv_prepare_step(arr, B, block_size, ptr(out["input_ids"]), ptr(out["positions"]),
+                                ptr(out["cu_seqlens_q"]), ptr(out["cu_seqlens_k"]),
+                                ptr(out["slot_mapping"]), ptr(out["context_lens"]),
+                                ptr(out["seq_need_compute_logits"]),
+                                ptr(out["block_tables"]), sizes.num_tokens, sizes.num_slots,
+                                B * w, ctypes.byref(sizes)))
+    out["max_seqlen_q"] = int(sizes.max_seqlen_q)
+    out["max_seqlen_k"] = int(sizes.max_seqlen_k)
+    return out

@@ -18,6 +18,8 @@ Cases (one JSON line each; bytes/flops are the algorithmic figures):
                   call, with the decode-only and prefill-only parts     (mixed)
   block_manager   host KV block manager: 256 x 1024-token prompts (half
                   sharing a 512-token prefix) admitted, then decode steps (host)
+  step_prepare    host step metadata (prepare_model_input): config 4's decode
+                  step and a 16 x 1024 prefill step                     (host)
 Inputs of every HBM case exceed L2 or are rotated through enough copies
 that each timed launch reads cold data.
 """
@@ -306,6 +308,64 @@ def case_block_manager(iters, B=256, prompt=1024, shared=512, page=256, steps=64
                 decode_step_batched_us=round(dec_b / steps * 1e6, 1), s=adm + dec, bound="host")
 
 
+def step_prepare_inputs(kind, B=256, page=256, seed=13):
+    """Sequence views of one step: "decode" = config 4's decode step (B
+    sequences, contexts U[1025, 1536], one new token each); "prefill" = 16
+    fresh 1024-token prompts."""
+    import ctypes
+    from ._lib import BlockSeq
+    rng = np.random.default_rng(seed)
+    if kind == "decode":
+        ctx = rng.integers(1025, 1537, B)
+        new = np.ones(B, np.int64)
+    else:
+        ctx = np.full(16, 1024)
+        new = ctx.copy()
+    keep, seqs = [], []
+    perm = rng.permutation(int(((ctx + page - 1) // page).sum()) + 8).astype(np.uint32)
+    used = 0
+    for L, n in zip(ctx, new):
+        toks = rng.integers(0, 151936, int(L)).astype(np.uint32)
+        nb = (int(L) + page - 1) // page
+        table = np.ascontiguousarray(perm[used:used + nb])
+        used += nb
+        keep += [toks, table]
+        seqs.append(BlockSeq(toks.ctypes.data, int(L), int(L - n), int(n), table.ctypes.data, nb,
+                             nb))
+    arr = (BlockSeq * len(seqs))(*seqs)
+    return arr, keep, [(t, tb) for t, tb in zip(keep[0::2], keep[1::2])], ctx, new
+
+
+def case_step_prepare(iters, reps=200):
+    """nvkv_prepare_step (host): config 4's 256-sequence decode step and a
+    16 x 1024 prefill step, outputs in preallocated host buffers; host clock,
+    mean over `reps` calls (ctypes adds ~1 us per call)."""
+    import ctypes
+    import time
+    from ._lib import StepSizes, lib
+    res = {}
+    for kind in ("decode", "prefill"):
+        arr, keep, _, ctx, new = step_prepare_inputs(kind)
+        B = len(arr)
+        sz = StepSizes()
+        assert lib.nvkv_prepare_step(arr, B, 256, None, None, None, None, None, None, None, None,
+                                     0, 0, 0, ctypes.byref(sz)) == 0
+        bufs = [np.zeros(max(int(n), 1), dt) for n, dt in
+                ((sz.num_tokens, np.int64), (sz.num_tokens, np.int64), (B + 1, np.uint32),
+                 (B + 1, np.uint32), (sz.num_slots, np.int64), (B, np.int64),
+                 (sz.num_need_logits, np.int64), (B * sz.block_table_width, np.uint32))]
+        args = [b.ctypes.data for b in bufs]
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            rc = lib.nvkv_prepare_step(arr, B, 256, *args, bufs[0].size, bufs[4].size,
+                                       bufs[7].size, ctypes.byref(sz))
+        dt = (time.perf_counter() - t0) / reps
+        assert rc == 0
+        res[kind + "_us"] = round(dt * 1e6, 2)
+        res[kind + "_tokens"] = int(sz.num_tokens)
+    return dict(kernel="prepare_step (host C++)", **res, s=res["decode_us"] * 1e-6, bound="host")
+
+
 CASES = {
     "store_cfg2": lambda it: case_store(72, 8, it),
     "store_prefill": lambda it: case_store(16384, 0, it),
@@ -328,6 +388,7 @@ CASES = {
     "mixed_4b_tp1": lambda it: case_mixed(it, 1),
     "mixed_4b_tp2": lambda it: case_mixed(it, 2),
     "block_manager": lambda it: case_block_manager(it),
+    "step_prepare": lambda it: case_step_prepare(it),
 }
 
 
