@@ -384,6 +384,7 @@ extern "C" int nvkv_comm_destroy(nvkv_comm_t c) {
 extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hidden,
                                        void* residual, int residual_mode, const void* weight,
                                        float eps, void* out, int dtype, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_allreduce_rms_norm");
   using namespace nvkv;
   clear_error();
   if (!c) return set_error(NVKV_ERR_INVALID_ARG, "allreduce_rms_norm: null comm");

@@ -119,6 +119,7 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
                          int max_seqlen_k, int num_q_heads, int num_kv_heads, int head_dim,
                          int page_size, float softmax_scale, int causal, void* workspace,
                          size_t workspace_bytes, int dtype, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_paged_attention");
   using namespace nvkv;
   clear_error();
   if (dtype != NVKV_DTYPE_BF16 && dtype != NVKV_DTYPE_F16)
@@ -264,6 +265,7 @@ int nvkv_attention_forward(nvkv_attention_t attn, const void* q, int64_t q_strid
                            int64_t k_stride, const void* v, int64_t v_stride,
                            int64_t num_tokens, int num_q_heads, int num_kv_heads, void* out,
                            int dtype, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_attention_forward");
   using namespace nvkv;
   clear_error();
   if (!attn) return set_error(NVKV_ERR_INVALID_ARG, "attention_forward: null attention");

@@ -313,6 +313,7 @@ int nvkv_block_manager_get_token_layout(nvkv_block_manager_t m, const nvkv_block
 // allocate (block_manager.rs:136-190): prefix-cache hits first, then fresh
 // blocks from the front of the free list for the num_new_tokens after them.
 int nvkv_block_manager_allocate(nvkv_block_manager_t m, nvkv_block_seq* s) {
+  NVKV_RANGE("nvkv_block_manager_allocate");
   using namespace nvkv;
   clear_error();
   int rc = check_seq(m, s, "block_manager_allocate");
@@ -381,6 +382,7 @@ int nvkv_block_manager_allocate(nvkv_block_manager_t m, nvkv_block_seq* s) {
 
 // deallocate (block_manager.rs:193-204): a finished or preempted sequence.
 int nvkv_block_manager_deallocate(nvkv_block_manager_t m, nvkv_block_seq* s) {
+  NVKV_RANGE("nvkv_block_manager_deallocate");
   using namespace nvkv;
   clear_error();
   int rc = check_seq(m, s, "block_manager_deallocate");
@@ -427,6 +429,7 @@ int nvkv_block_manager_can_append(nvkv_block_manager_t m, const nvkv_block_seq* 
 // may_append (block_manager.rs:222-284): blocks and hashes for the
 // num_new_tokens after num_cached_tokens of a running sequence.
 int nvkv_block_manager_may_append(nvkv_block_manager_t m, nvkv_block_seq* s) {
+  NVKV_RANGE("nvkv_block_manager_may_append");
   using namespace nvkv;
   clear_error();
   int rc = check_seq(m, s, "block_manager_may_append");
@@ -536,6 +539,7 @@ extern "C" {
 // sequence unchanged.
 int nvkv_block_manager_append_batch(nvkv_block_manager_t m, nvkv_block_seq* seqs, int64_t n,
                                     const int64_t* num_new_tokens, int64_t* done) {
+  NVKV_RANGE("nvkv_block_manager_append_batch");
   using namespace nvkv;
   clear_error();
   if (!m || !done || n < 0 || (n > 0 && (!seqs || !num_new_tokens)))

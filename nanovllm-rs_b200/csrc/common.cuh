@@ -23,7 +23,21 @@
 #error "nvkv is written for sm_100a only"
 #endif
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace nvkv {
+
+// NVTX range for the lifetime of a host call (a profiler shows one range per
+// C-ABI call, named after the entry point; without one attached the NVTX3
+// calls return at once).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define NVKV_RANGE(name) ::nvkv::NvtxRange nvkv_nvtx_range_(name)
+
 
 // ---------------------------------------------------------------------------
 // Host status plumbing

@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
 extern "C" int nvkv_rms_norm(const void* x, int64_t x_stride, void* residual, int64_t res_stride,
                              const void* weight, float eps, void* out, int64_t out_stride,
                              int64_t num_tokens, int hidden, int dtype, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_rms_norm");
   using namespace nvkv;
   clear_error();
   if (dtype != NVKV_DTYPE_BF16 && dtype != NVKV_DTYPE_F16)
@@ -91,6 +92,7 @@ extern "C" int nvkv_rms_norm(const void* x, int64_t x_stride, void* residual, in
 extern "C" int nvkv_silu_and_mul(const void* gate_up, int64_t gu_stride, void* out,
                                  int64_t out_stride, int64_t num_tokens, int inter, int dtype,
                                  nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_silu_and_mul");
   using namespace nvkv;
   clear_error();
   if (dtype != NVKV_DTYPE_BF16 && dtype != NVKV_DTYPE_F16)

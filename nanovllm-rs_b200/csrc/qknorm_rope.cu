@@ -148,6 +148,7 @@ extern "C" int nvkv_qknorm_rope(const void* qkv, int64_t qkv_stride, int64_t num
                                 int64_t max_position, void* q_out, void* k_out, void* v_out,
                                 void* k_cache, void* v_cache, const int64_t* slot_mapping,
                                 int64_t num_slots, int dtype, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_qknorm_rope");
   using namespace nvkv;
   clear_error();
   if (dtype != NVKV_DTYPE_BF16 && dtype != NVKV_DTYPE_F16)

@@ -78,6 +78,7 @@ extern "C" int nvkv_decode_advance(int num_seqs, int page_size, int64_t* seq_len
                                    int64_t num_blocks, int64_t* positions,
                                    int64_t* slot_mapping, uint32_t* cu_seqlens_q,
                                    uint32_t* cu_seqlens_k, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_decode_advance");
   using namespace nvkv;
   clear_error();
   if (num_seqs < 0 || page_size <= 0 || block_table_stride <= 0 || num_blocks <= 0)

@@ -16,6 +16,7 @@ int nvkv_prepare_step(const nvkv_block_seq* seqs, int64_t num_seqs, int64_t bloc
                       uint32_t* cu_seqlens_k, int64_t* slot_mapping, int64_t* context_lens,
                       int64_t* need_logits, uint32_t* block_tables, int64_t capacity_tokens,
                       int64_t capacity_slots, int64_t capacity_table, nvkv_step_sizes* sizes) {
+  NVKV_RANGE("nvkv_prepare_step");
   using namespace nvkv;
   clear_error();
   if (!sizes || num_seqs < 0 || block_size <= 0 || (num_seqs > 0 && !seqs))

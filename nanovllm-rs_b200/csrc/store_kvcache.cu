@@ -121,6 +121,7 @@ extern "C" int nvkv_store_kvcache(const void* key, const void* value, void* k_ca
                                   void* v_cache, const int64_t* slot_mapping, int64_t num_tokens,
                                   int64_t row_elems, int64_t key_stride, int64_t value_stride,
                                   int64_t num_slots, int dtype, nvkv_stream_t stream) {
+  NVKV_RANGE("nvkv_store_kvcache");
   using namespace nvkv;
   clear_error();
   if (dtype != NVKV_DTYPE_BF16 && dtype != NVKV_DTYPE_F16)
