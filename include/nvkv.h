@@ -439,6 +439,23 @@ int nvkv_prepare_step(const nvkv_block_seq* seqs, int64_t num_seqs, int64_t bloc
                       int64_t* need_logits, uint32_t* block_tables, int64_t capacity_tokens,
                       int64_t capacity_slots, int64_t capacity_table, nvkv_step_sizes* sizes);
 
+/* ------------------------------------------------------------------------
+ * KV-pool sizing: ModelRunner::probe_num_kvcache_blocks
+ * (engine/model_runner.rs:264-284).  num_blocks = max((i64)(total *
+ * utilization) - (total - free), 0) / (2 * num_layers * block_size *
+ * num_kv_heads * head_dim * dtype_bytes), num_kv_heads per rank; 0 blocks
+ * is an error (the reference asserts).  nvkv_kv_pool_probe reads free and
+ * total from cudaMemGetInfo on the current device.  Under tensor
+ * parallelism the caller takes the minimum over ranks, as the reference
+ * requires before allocating.  The pool itself is 2 x num_layers tensors of
+ * [num_blocks, block_size, num_kv_heads, head_dim] (model_runner.rs:286-303).
+ * ---------------------------------------------------------------------- */
+int nvkv_kv_pool_blocks(int64_t free_bytes, int64_t total_bytes, double gpu_memory_utilization,
+                        int num_layers, int block_size, int num_kv_heads, int head_dim,
+                        int dtype_bytes, int64_t* num_blocks);
+int nvkv_kv_pool_probe(double gpu_memory_utilization, int num_layers, int block_size,
+                       int num_kv_heads, int head_dim, int dtype_bytes, int64_t* num_blocks);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,6 +108,8 @@ SIGNATURES = {
     "nvkv_block_manager_block_info": [_p, _i64, _pi64, _pi64, _pi64, _pi32],
     "nvkv_block_manager_free_ids": [_p, _p, _i64, _pi64],
     "nvkv_block_manager_lookup": [_p, _i64, _pi64],
+    "nvkv_kv_pool_blocks": [_i64, _i64, ctypes.c_double, _i32, _i32, _i32, _i32, _i32, _pi64],
+    "nvkv_kv_pool_probe": [ctypes.c_double, _i32, _i32, _i32, _i32, _i32, _pi64],
     "nvkv_prepare_step": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                           ctypes.POINTER(StepSizes)],
 }

@@ -214,3 +214,34 @@ def prepare_step(seqs, block_size: int) -> dict:
     out["max_seqlen_q"] = int(sizes.max_seqlen_q)
     out["max_seqlen_k"] = int(sizes.max_seqlen_k)
     return out
+
+
+def kv_pool_blocks(free_bytes: int, total_bytes: int, gpu_memory_utilization: float,
+                   num_layers: int, block_size: int, num_kv_heads: int, head_dim: int,
+                   dtype_bytes: int) -> int:
+    """ModelRunner::probe_num_kvcache_blocks (engine/model_runner.rs:264-284)
+    for given free / total device bytes; raises when no block fits."""
+    out = ctypes.c_int64(0)
+    check(lib.nvkv_kv_pool_blocks(free_bytes, total_bytes, gpu_memory_utilization, num_layers,
+                                  block_size, num_kv_heads, head_dim, dtype_bytes,
+                                  ctypes.byref(out)))
+    return int(out.value)
+
+
+def kv_pool_probe(gpu_memory_utilization: float, num_layers: int, block_size: int,
+                  num_kv_heads: int, head_dim: int, dtype_bytes: int, group=None) -> int:
+    """The same on the current device (cudaMemGetInfo); with a process group,
+    the minimum over its ranks (the reconciliation the reference requires
+    before allocating)."""
+    out = ctypes.c_int64(0)
+    check(lib.nvkv_kv_pool_probe(gpu_memory_utilization, num_layers, block_size, num_kv_heads,
+                                 head_dim, dtype_bytes, ctypes.byref(out)))
+    n = int(out.value)
+    if group is not None:
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([n], dtype=torch.int64,
+                         device="cuda" if dist.get_backend(group) == "nccl" else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+        n = int(t.item())
+    return n
