@@ -236,12 +236,17 @@ def kv_pool_probe(gpu_memory_utilization: float, num_layers: int, block_size: in
     out = ctypes.c_int64(0)
     check(lib.nvkv_kv_pool_probe(gpu_memory_utilization, num_layers, block_size, num_kv_heads,
                                  head_dim, dtype_bytes, ctypes.byref(out)))
-    n = int(out.value)
-    if group is not None:
-        import torch
-        import torch.distributed as dist
-        t = torch.tensor([n], dtype=torch.int64,
-                         device="cuda" if dist.get_backend(group) == "nccl" else "cpu")
-        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
-        n = int(t.item())
-    return n
+    return kv_pool_reconcile(int(out.value), group)
+
+
+def kv_pool_reconcile(num_blocks: int, group=None) -> int:
+    """The minimum of every rank's block budget (every rank must allocate the
+    same pool, model_runner.rs:265-266)."""
+    if group is None:
+        return num_blocks
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([num_blocks], dtype=torch.int64,
+                     device="cuda" if dist.get_backend(group) == "nccl" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return int(t.item())

@@ -97,3 +97,33 @@ def test_divide_rejects_uneven_heads():
     assert divide(32, 8) == 4
     with pytest.raises(ValueError):
         divide(8, 3)
+
+
+def _pool_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from nvkv.blocks import kv_pool_reconcile
+        got = kv_pool_reconcile([900, 750][rank], dist.group.WORLD)
+        q.put((rank, got))
+    except Exception as ex:  # pragma: no cover - reported through the queue
+        q.put((rank, repr(ex)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_kv_pool_budget_is_the_minimum_over_ranks():
+    """Every rank allocates the same pool: the smallest rank budget
+    (model_runner.rs:265-266), reconciled over the process group."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pool_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(60)
+    assert res == {0: 750, 1: 750}, res
