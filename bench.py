@@ -53,6 +53,21 @@ def parse():
     return ap.parse_args()
 
 
+def bench_config(world, cuda_graph=True, nccl_allreduce=False):
+    """The `config` object of both arms' JSON lines (the same workload)."""
+    return {
+        "workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256, all 36 layers + "
+                    "lm_head + vocab-parallel argmax; attention path = nvkv kernels, GEMMs = "
+                    "cuBLAS, TP all-reduce + RMSNorm = nvkv peer-memory kernel (NCCL with "
+                    "--nccl-allreduce), greedy-pick all-gather = NCCL",
+        "model": "Qwen3-8B", "global_batch": NUM_SEQS, "seq_len": PROMPT + MAX_OUT,
+        "parallelism": f"tp{world}", "cuda_graph": bool(cuda_graph),
+        "allreduce_route": ("none" if world == 1 else
+                            "nccl + nvkv_rms_norm" if nccl_allreduce else "nvkv_allreduce_rms_norm"),
+        "l2": "inputs larger than L2 (per-step KV read >> 126 MB), no flush",
+    }
+
+
 def workload(seed=SEED):
     """Seeded decode-step metadata, built like ModelRunner::prepare_model_input
     (model_runner.rs:82-131) for 256 sequences each decoding one token."""
@@ -404,18 +419,8 @@ def run_nvkv(a):
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, random prefilled KV, random token ids)",
-            "config": {
-                "workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256, all 36 "
-                            "layers + lm_head + vocab-parallel argmax; attention path = nvkv kernels, GEMMs = "
-                            "cuBLAS, TP all-reduce + RMSNorm = nvkv peer-memory kernel (NCCL "
-                            "with --nccl-allreduce), greedy-pick all-gather = NCCL",
-                "model": "Qwen3-8B", "global_batch": NUM_SEQS, "seq_len": int(w["max_k"]),
-                "parallelism": f"tp{world}", "cuda_graph": graph is not None,
-                "allreduce_route": ("none" if world == 1 else
-                                    "nccl + nvkv_rms_norm" if model.comm is None else
-                                    "nvkv_allreduce_rms_norm"),
-                "l2": "inputs larger than L2 (per-step KV read >> 126 MB), no flush",
-            },
+            "config": bench_config(world, cuda_graph=graph is not None,
+                                   nccl_allreduce=model.comm is None),
             "e2e": {"value": round(NUM_SEQS * a.steps / (ms_e2e * 1e-3), 1), "unit": "tok/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": NUM_SEQS * 8},
             "gpu_launches": int(launches),
@@ -431,9 +436,8 @@ def run_nvkv(a):
         if ar is not None:
             line["collectives"] = ar
         if world == 1:
-            line["cpu_baseline"] = cpu_reference(max_seconds=20.0)
+            line["cpu_baseline"] = cpu_reference()
             line["op_level"] = op_level_config2()
-            line["block_manager"] = block_manager_host()
         print(json.dumps(line), flush=True)
     # a graph holding NCCL calls must be released before the process group
     run = None
@@ -458,56 +462,11 @@ def run_nvkv(a):
 
 # ---------------------------------------------------------------------------
 # CPU restatement of the reference path (the reference's candle-CPU route is
-# not buildable here: Rust toolchain absent), timed on the host cores.
+# not buildable here: Rust toolchain absent), timed on the host cores.  This
+# part imports neither torch's CUDA side nor nvkv: the oracle is numpy.
 # ---------------------------------------------------------------------------
 
-def _cpu_sample_setup(num_tokens=32, layers=2, vocab_frac=32, seed=7):
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import nvkv_oracle as O
-    from qwen3_cpu import Qwen3CPU
-    from nvkv.decoder import QWEN3_8B
-    from dataclasses import replace
-
-    cfg = replace(QWEN3_8B, num_hidden_layers=layers)
-    rng = np.random.default_rng(seed)
-    H, D, F = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
-    hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
-
-    base = rng.standard_normal(1 << 20, dtype=np.float32)
-
-    def r(*shape, s=0.02):  # timing only: tile one seeded random buffer
-        n = int(np.prod(shape))
-        off = int(rng.integers(0, 1 << 19))
-        return (np.resize(np.roll(base, off), n) * np.float32(s)).reshape(shape)
-
-    wts = {"embed": r(cfg.vocab_size // vocab_frac, H, s=1.0), "norm": np.ones(H, np.float32),
-           "lm_head": r(cfg.vocab_size // vocab_frac, H)}
-    for i in range(layers):
-        wts.update({f"{i}.qkv": r((hq + 2 * hkv) * D, H), f"{i}.o": r(H, hq * D),
-                    f"{i}.gate_up": r(2 * F, H), f"{i}.down": r(H, F),
-                    f"{i}.ln1": np.ones(H, np.float32), f"{i}.ln2": np.ones(H, np.float32),
-                    f"{i}.qn": np.ones(D, np.float32), f"{i}.kn": np.ones(D, np.float32)})
-    w = workload()
-    ctx_lens = w["ctx"][:num_tokens]
-    nblk = (ctx_lens + PAGE - 1) // PAGE
-    model = Qwen3CPU(cfg, wts, int(nblk.sum()), PAGE)
-    for kc, vc in zip(model.k, model.v):
-        kc[...] = r(*kc.shape, s=1.0)
-        vc[...] = r(*vc.shape, s=1.0)
-    seqs, used = [], 0
-    for L, n in zip(ctx_lens, nblk):
-        seqs.append(O.Seq(list(rng.integers(0, 1000, int(L))), list(range(used, used + n)),
-                          int(L) - 1, 1, PAGE))
-        used += n
-    ids, pos, ctx = O.prepare_model_input(seqs, PAGE)
-    ids = ids % wts["embed"].shape[0]
-    return model, ids, pos, ctx, cfg
-
-
-def _cpu_one(model, ids, pos, ctx):
-    t0 = time.perf_counter()
-    model.forward(ids, pos, ctx)
-    return time.perf_counter() - t0
+CPU_SAMPLE_SEQS = 16
 
 
 def _all_host_threads():
@@ -523,90 +482,100 @@ def _all_host_threads():
     return n
 
 
-def block_manager_host(B=256, prompt=1024, shared=512, page=256, steps=64):
-    """The KV block manager on the host (config 4's shape: 256 sequences x
-    1024-token prompts, P=256, half sharing a 512-token prefix): admission
-    (get_token_layout, can_allocate, allocate) and `steps` decode steps
-    (can_append, may_append) through the C ABI, next to the Python
-    restatement of the reference's manager (oracle, one thread) on the same
-    workload.  Host clock; the reference's own manager is compiled Rust, so
-    the port's time is a baseline, not the reference's speed."""
-    try:
-        from nvkv import kbench
-        c = kbench.case_block_manager(1, B=B, prompt=prompt, shared=shared, page=page, steps=steps)
+class CpuDecodeSample:
+    """The reference's CPU route (candle CPU fp32: GEMMs, paged gather, unfused
+    causal attention; oracle/qwen3_cpu.py) on a bounded sample of the bench
+    workload: the first `num_seqs` of its 256 sequences (same seeded contexts,
+    U[1025,1536]), each decoding one token through all 36 Qwen3-8B layers,
+    the final norm and the full-vocab lm_head.  Every sequence has its own
+    paged KV per layer, filled with random values.
+
+    The 36 layers share one random-init fp32 weight set (0.77 GB per layer,
+    far larger than the host caches, so each layer streams its weights from
+    DRAM exactly as distinct weights would) so the sample fits in host
+    memory; the embedding and lm_head are full size (2.5 GB each)."""
+
+    def __init__(self, num_seqs=CPU_SAMPLE_SEQS, seed=7):
+        from concurrent.futures import ThreadPoolExecutor
+
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import block_manager_oracle as OB
-        rng = np.random.default_rng(12)
-        pre = [int(t) for t in rng.integers(0, 151936, shared)]
-        nb = B * ((prompt + steps + page - 1) // page) + 8
-        bm = OB.BlockManager(nb, page)
-        seqs = []
-        for b in range(B):
-            toks = [int(t) for t in rng.integers(0, 151936, prompt)]
-            if b % 2 == 0:
-                toks[:shared] = pre
-            seqs.append(OB.Seq(toks, page))
+        sys.path.insert(0, os.path.join(ROOT, "nanovllm-rs_b200"))
+        import nvkv_oracle as O
+        from qwen3_cpu import Qwen3CPU
+        from qwen3_config import QWEN3_8B
+
+        self.cores = _all_host_threads()
+        cfg = self.cfg = QWEN3_8B
+        self.num_seqs = num_seqs
+        rng = np.random.default_rng(seed)
+        H, D, F = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
+        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        base = rng.standard_normal(1 << 22, dtype=np.float32)
+        pool = ThreadPoolExecutor(self.cores)
+
+        def fill(out, s):  # timing only: one seeded random buffer, tiled, on all cores
+            src = np.roll(base, int(rng.integers(0, base.size))) * np.float32(s)
+            flat = out.reshape(-1)
+
+            def part(i):
+                n = min(base.size, flat.size - i)
+                flat[i:i + n] = src[:n]
+
+            list(pool.map(part, range(0, flat.size, base.size)))
+            return out
+
+        def r(*shape, s=0.02):
+            return fill(np.empty(shape, np.float32), s)
+
+        layer = {"qkv": r((hq + 2 * hkv) * D, H), "o": r(H, hq * D), "gate_up": r(2 * F, H),
+                 "down": r(H, F), "ln1": np.ones(H, np.float32), "ln2": np.ones(H, np.float32),
+                 "qn": np.ones(D, np.float32), "kn": np.ones(D, np.float32)}
+        wts = {"embed": r(cfg.vocab_size, H, s=1.0), "norm": np.ones(H, np.float32),
+               "lm_head": r(cfg.vocab_size, H)}
+        for i in range(cfg.num_hidden_layers):
+            for k, v in layer.items():
+                wts[f"{i}.{k}"] = v
+        w = workload()
+        ctx_lens = w["ctx"][:num_seqs]
+        nblk = (ctx_lens + PAGE - 1) // PAGE
+        self.model = Qwen3CPU(cfg, wts, int(nblk.sum()), PAGE)
+        for kc, vc in zip(self.model.k, self.model.v):
+            fill(kc, 1.0)
+            fill(vc, 1.0)
+        self.model.pool = pool
+        seqs, used = [], 0
+        for L, n in zip(ctx_lens, nblk):
+            seqs.append(O.Seq(list(rng.integers(0, cfg.vocab_size, int(L))),
+                              list(range(used, used + n)), int(L) - 1, 1, PAGE))
+            used += n
+        self.ids, self.pos, self.ctx = O.prepare_model_input(seqs, PAGE)
+        self.kv_bytes = int(ctx_lens.sum()) * hkv * D * 2 * 4 * cfg.num_hidden_layers
+
+    def step(self) -> float:
+        """One sampled decode step (all layers, lm_head, argmax); host seconds."""
         t0 = time.perf_counter()
-        for s in seqs:
-            _, free, new = bm.get_token_layout(s)
-            bm.can_allocate(free + new)
-            s.num_new_tokens = new
-            bm.allocate(s)
-            s.num_cached_tokens += s.num_new_tokens
-            s.num_new_tokens = 0
-        t1 = time.perf_counter()
-        for _ in range(steps):
-            for s in seqs:
-                s.append_token(7)
-                bm.can_append(s, 1)
-                s.num_new_tokens = 1
-                bm.may_append(s)
-                s.num_cached_tokens += 1
-                s.num_new_tokens = 0
-        t2 = time.perf_counter()
-        port = {"admission_us_per_seq": round((t1 - t0) / B * 1e6, 2),
-                "decode_step_us": round((t2 - t1) / steps * 1e6, 1), "cores": 1,
-                "kind": "port", "sample": "the same workload, Python restatement "
-                                          "(oracle/block_manager_oracle.py)"}
-        return {"workload": f"{B} seqs x {prompt}-token prompts, P={page}, half sharing a "
-                            f"{shared}-token prefix; admission + {steps} decode steps",
-                "nvkv": {"admission_us_per_seq": c["admission_us_per_seq"],
-                         "decode_step_us": c["decode_step_us"],
-                         "decode_step_batched_us": c["decode_step_batched_us"],
-                         "note": "C ABI via ctypes (~1 us per call included); batched = "
-                                 "nvkv_block_manager_append_batch, one call per step"},
-                "cpu_port": port,
-                "admission_speedup_vs_port": round(port["admission_us_per_seq"]
-                                                   / c["admission_us_per_seq"], 1),
-                "decode_step_speedup_vs_port": round(port["decode_step_us"]
-                                                     / c["decode_step_batched_us"], 1),
-                "prepare_step": _prepare_step_host()}
-    except Exception as e:  # a side measurement never breaks the bench line
-        return {"error": f"{type(e).__name__}: {e}"}
+        logits = self.model.forward(self.ids, self.pos, self.ctx)
+        np.argmax(logits, axis=-1)
+        return time.perf_counter() - t0
+
+    def describe(self, steps):
+        return (f"{self.num_seqs} of the 256 sequences (contexts {int(self.ctx.max_seqlen_k)} max), "
+                f"one decode token each through all {self.cfg.num_hidden_layers} layers + full "
+                f"lm_head + argmax per step, {steps} timed steps; numpy fp32 restatement of the "
+                f"reference's CPU route (oracle/qwen3_cpu.py), one weight set shared by the "
+                f"layers, own paged KV per layer and sequence")
 
 
-def _prepare_step_host():
-    """prepare_model_input on the host: nvkv_prepare_step (C ABI) against the
-    oracle's restatement, on config 4's decode step and a 16 x 1024 prefill."""
-    from nvkv import kbench
-    import nvkv_oracle as O
-    c = kbench.case_step_prepare(1)
-    port = {}
-    for kind in ("decode", "prefill"):
-        arr, keep, pairs, ctx, new = kbench.step_prepare_inputs(kind)
-        seqs = [O.Seq([int(t) for t in toks], [int(b) for b in table], int(L - n), int(n), 256)
-                for (toks, table), L, n in zip(pairs, ctx, new)]
-        reps = 5
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            O.prepare_model_input(seqs, 256)
-        port[kind + "_us"] = round((time.perf_counter() - t0) / reps * 1e6, 1)
-    return {"nvkv": {k: c[k] for k in ("decode_us", "prefill_us", "decode_tokens",
-                                       "prefill_tokens")},
-            "cpu_port": dict(port, cores=1, kind="port",
-                             sample="oracle prepare_model_input, same steps"),
-            "decode_speedup_vs_port": round(port["decode_us"] / c["decode_us"], 1),
-            "prefill_speedup_vs_port": round(port["prefill_us"] / c["prefill_us"], 1)}
+def cpu_reference(steps=3, warmup=1, num_seqs=CPU_SAMPLE_SEQS):
+    """The `cpu_baseline` of the GPU arm's line: `steps` sampled decode steps
+    (CpuDecodeSample) after `warmup`, tok/s = sampled tokens / host time."""
+    smp = CpuDecodeSample(num_seqs)
+    for _ in range(warmup):
+        smp.step()
+    t = sum(smp.step() for _ in range(steps))
+    return {"value": round(num_seqs * steps / t, 3), "unit": "tok/s", "cores": smp.cores,
+            "kind": "port", "sample": smp.describe(steps),
+            "ms_per_step": round(t / steps * 1e3, 1)}
 
 
 def op_level_config2(seed=2, reps=20):
@@ -725,65 +694,29 @@ def op_level_config2(seed=2, reps=20):
     return res
 
 
-def cpu_reference(max_seconds=20.0, reps=None, warmup=1, num_tokens=32, layers=2, vocab_frac=32):
-    """Times the CPU restatement on a bounded sample of the same decode step:
-    `num_tokens` of the 256 sequences through `layers` of the 36 layers and a
-    1/`vocab_frac` slice of lm_head; the step time is scaled by
-    (256/num_tokens) * (36/layers) for the layers and likewise for the head."""
-    _all_host_threads()
-    model, ids, pos, ctx, cfg = _cpu_sample_setup(num_tokens, layers, vocab_frac)
-    for _ in range(warmup):
-        _cpu_one(model, ids, pos, ctx)
-    times, t_start = [], time.perf_counter()
-    while True:
-        times.append(_cpu_one(model, ids, pos, ctx))
-        if reps is not None and len(times) >= reps:
-            break
-        if reps is None and time.perf_counter() - t_start >= max_seconds:
-            break
-    t = statistics.median(times)
-    # split the sample time: lm_head slice measured alone, the rest is layers
-    h = np.zeros((num_tokens, cfg.hidden_size), np.float32)
-    t0 = time.perf_counter()
-    for _ in range(3):
-        h @ model.w["lm_head"].T
-    t_head = (time.perf_counter() - t0) / 3
-    t_layers = max(t - t_head, 0.0)
-    step = (t_layers * (36 / layers) + t_head * vocab_frac) * (NUM_SEQS / num_tokens)
-    try:
-        import threadpoolctl
-        cores = max(i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()) or 1
-    except Exception:
-        cores = os.cpu_count()
-    return {"value": round(NUM_SEQS / step, 2), "unit": "tok/s", "cores": int(cores),
-            "kind": "port",
-            "sample": f"{num_tokens} of 256 decode tokens x {layers} of 36 layers + 1/{vocab_frac} "
-                      f"lm_head, numpy fp32 restatement (oracle/qwen3_cpu.py), median of "
-                      f"{len(times)} reps, scaled to the full step",
-            "sample_s_per_rep": round(t, 4)}
-
-
 def run_reference(a):
+    """The reference arm: the CPU restatement of the reference's route on the
+    host cores, on this bench's `config`, metric and unit.  Each step is one
+    CpuDecodeSample step (a bounded sample of the workload, really run); the
+    line's value is sampled tokens / host time over exactly `--steps` steps.
+    Under torchrun only rank 0 runs; the other ranks exit at once."""
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if rank != 0:
         return
-    _all_host_threads()
-    model, ids, pos, ctx, cfg = _cpu_sample_setup()
-    for _ in range(max(a.warmup, 1)):
-        _cpu_one(model, ids, pos, ctx)
-    cb = cpu_reference(reps=max(1, min(a.steps, 30)), warmup=0)
-    val = cb["value"]
-    line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(NUM_SEQS / val * 1e3, 3),
+    smp = CpuDecodeSample()
+    for _ in range(a.warmup):
+        smp.step()
+    t = sum(smp.step() for _ in range(a.steps))
+    val = smp.num_seqs * a.steps / t
+    line = {"metric": METRIC, "value": round(val, 3), "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t / a.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "Qwen3-8B decode step, 256 seqs, ctx U[1025,1536], P=256 "
-                                   "(bounded CPU sample, scaled)", "model": "Qwen3-8B",
-                       "global_batch": NUM_SEQS, "seq_len": PROMPT + MAX_OUT,
-                       "parallelism": "cpu"},
-            "cpu_baseline": cb,
-            "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0,
+            "data": "synthetic (seeded random-init weights, random prefilled KV, random token ids)",
+            "impl": "reference", "config": bench_config(world),
+            "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": smp.cores,
+                             "kind": "port", "sample": smp.describe(a.steps)},
+            "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

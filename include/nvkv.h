@@ -122,8 +122,15 @@ int nvkv_qknorm_rope(const void* qkv, int64_t qkv_stride, int64_t num_tokens, in
  *           window (None, Some(0)) and flash_attn_varlen(causal=true)).
  *
  * q:   [num_q_tokens, Hq, D] with token stride q_stride (elements); head
- *      stride D.  num_q_tokens bounds every read of q.
+ *      stride D.
  * out: [num_q_tokens, Hq, D] contiguous.
+ * Device-side checks (the metadata lives on the device, so the host cannot
+ * see it): a sequence whose query rows cu_seqlens_q[b] .. cu_seqlens_q[b+1]
+ * reach past num_q_tokens, whose k_len exceeds max_seqlen_k, or (q_len > 1)
+ * whose k_len is below its q_len is skipped -- none of its q rows are read,
+ * none of its out rows written, no block-table entry beyond max_seqlen_k keys
+ * read -- and NVKV_DEVERR_SEQLEN is recorded for nvkv_device_error().  A page id >=
+ * num_blocks reads page 0 instead and records NVKV_DEVERR_BLOCK_RANGE.
  * Paged (block_tables != NULL): k_cache/v_cache are [num_blocks, page_size,
  *      Hkv, D]; key j of sequence b lives in page block_tables[b *
  *      block_table_stride + j / page_size], row j % page_size.
@@ -172,8 +179,12 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
  * are rejected with NVKV_ERR_WORKSPACE.  All calls share that array (it keeps
  * the last call's contents; nothing needs to start zeroed), so calls that
  * overlap on the GPU race: serialise them.  The first call on a device looks
- * the array's address up once; make it before any stream capture.  Calls no
- * cudaMalloc/cudaFree.
+ * the array's address up once, which (with CUDA's lazy module loading) is
+ * also when the array takes its device memory: make that call before any
+ * stream capture and before sizing the KV pool from free memory
+ * (nvkv_kv_pool_probe); a call with num_seqs == 0 does only this set-up.  The
+ * address is kept until exit, so a cudaDeviceReset after the first call is
+ * not supported.  Calls no cudaMalloc/cudaFree.
  * ---------------------------------------------------------------------- */
 #define NVKV_NOALLOC_SCRATCH_BYTES (4u << 20)
 

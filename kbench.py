@@ -1,6 +1,6 @@
 """Per-kernel microbenchmarks of the nvkv path (CUDA-event timed).
 
-    python -m nvkv.kbench [--case NAME ...] [--iters N]     (from nanovllm-rs_b200/)
+    python kbench.py [--case NAME ...] [--iters N]
 
 Cases (one JSON line each; bytes/flops are the algorithmic figures):
   store_cfg2      nvkv_store_kvcache: 64 tokens + 8 padded
@@ -29,12 +29,15 @@ import argparse
 import json
 import os
 
+import sys
+
 import numpy as np
 import torch
 
-from . import ops
+_ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(_ROOT, "nanovllm-rs_b200"))
 
-_ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from nvkv import ops  # noqa: E402
 
 
 def _peaks():
@@ -231,7 +234,7 @@ def case_block_manager(iters, B=256, prompt=1024, shared=512, page=256, steps=64
     timed beside it as the CPU baseline)."""
     import ctypes
     import time
-    from ._lib import BlockSeq, lib
+    from nvkv._lib import BlockSeq, lib
     rng = np.random.default_rng(12)
     pre = rng.integers(0, 151936, shared).astype(np.uint32)
     cap_tok = prompt + steps * iters + 8
@@ -313,7 +316,7 @@ def step_prepare_inputs(kind, B=256, page=256, seed=13):
     sequences, contexts U[1025, 1536], one new token each); "prefill" = 16
     fresh 1024-token prompts."""
     import ctypes
-    from ._lib import BlockSeq
+    from nvkv._lib import BlockSeq
     rng = np.random.default_rng(seed)
     if kind == "decode":
         ctx = rng.integers(1025, 1537, B)
@@ -342,7 +345,7 @@ def case_step_prepare(iters, reps=200):
     mean over `reps` calls (ctypes adds ~1 us per call)."""
     import ctypes
     import time
-    from ._lib import StepSizes, lib
+    from nvkv._lib import StepSizes, lib
     res = {}
     for kind in ("decode", "prefill"):
         arr, keep, _, ctx, new = step_prepare_inputs(kind)
@@ -421,7 +424,7 @@ def main(argv=None):
         r.pop("s")
         print(json.dumps(r), flush=True)
     if torch.cuda.is_available():
-        from ._lib import device_error
+        from nvkv._lib import device_error
         assert device_error() == 0
 
 

@@ -105,7 +105,6 @@ int launch_store_kvcache(const void* key, const void* value, void* k_cache, void
 // (PDL): the grid may be scheduled while that kernel drains, and the kernel
 // must execute griddepcontrol.wait (pdl_wait below) before it reads any
 // input.  After a non-kernel stream operation the attribute has no effect.
-// NVKV_NO_PDL turns the attribute off (A/B builds).
 #ifdef __CUDACC__
 template <typename... KArgs, typename... Args>
 int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -119,11 +118,7 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-#ifdef NVKV_NO_PDL
-  cfg.numAttrs = 0;
-#else
   cfg.numAttrs = 1;
-#endif
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
 }
 #endif

@@ -20,8 +20,13 @@
 //    before the combine reads it), but calls that overlap on the GPU (other
 //    streams, other threads) race on it -- serialise them;
 //  * the first call on a device looks the array's device address up
-//    (cudaGetSymbolAddress, once per device, with that device current), so
-//    make that first call before any stream capture.
+//    (cudaGetSymbolAddress, once per device, with that device current); with
+//    CUDA's lazy module loading that lookup is also when the 4 MiB are taken
+//    from the device.  Make that first call before any stream capture and
+//    before sizing the KV pool from free memory (nvkv_kv_pool_probe); a call
+//    with num_seqs == 0 does only this set-up;
+//  * the address is kept for the life of the process: a cudaDeviceReset
+//    after the first call is not supported.
 #include <mutex>
 
 #include "common.cuh"
@@ -81,13 +86,11 @@ extern "C" int nvkv_paged_attention_noalloc(
                          std::to_string(kNoAllocScratchBytes) +
                          "-byte static scratch; call nvkv_paged_attention with a workspace");
   void* ws = nullptr;
-  if (need > 0) {
-    rc = noalloc_scratch(&ws);
-    if (rc) return rc;
-  }
+  rc = noalloc_scratch(&ws);  // every call, so an empty first call is the set-up
+  if (rc) return rc;
   return nvkv_paged_attention(q, q_stride, num_q_tokens, k_cache, v_cache, num_blocks, kv_stride,
                               out, cu_seqlens_q, cu_seqlens_k, block_tables, block_table_stride,
                               num_seqs, max_seqlen_q, max_seqlen_k, num_q_heads, num_kv_heads,
-                              head_dim, page_size, softmax_scale, causal, ws,
-                              need > 0 ? kNoAllocScratchBytes : 0, dtype, stream);
+                              head_dim, page_size, softmax_scale, causal, ws, kNoAllocScratchBytes,
+                              dtype, stream);
 }

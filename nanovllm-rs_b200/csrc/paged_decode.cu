@@ -41,6 +41,7 @@ struct DecodeParams {
   int page_size;
   int chunk_tokens;  // keys per split, multiple of kDecTile
   int max_k;         // max_seqlen_k: the block tables cover this many keys
+  int64_t num_q_rows;  // rows of q and out
   int max_splits;
   float scale_log2;
   float* ws_o;    // [B][max_splits][Hq][D]
@@ -58,11 +59,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   uint64_t* empty = full + kDecStages;
   float* red = reinterpret_cast<float*>(empty + kDecStages);  // [warp][m|l][16]
 
-#ifdef NVKV_DECODE_SPLIT_MAJOR
-  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-#else
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -97,7 +94,9 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   const int k_len = (int)(p.cu_k[b + 1] - p.cu_k[b]);
   const int nsplit = k_len > 0 ? (k_len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
   if (split >= nsplit) return;
-  if (k_len > p.max_k) {  // beyond max_seqlen_k the block table may be shorter
+  // beyond max_seqlen_k the block table may be shorter; a row past the q/out
+  // buffers is neither read nor written
+  if (k_len > p.max_k || (int64_t)q0 >= p.num_q_rows) {
     if (threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
     return;
   }
@@ -229,7 +228,8 @@ __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParam
   if (p.cu_q[b + 1] - q0 != 1) return;
   const int k_len = (int)(p.cu_k[b + 1] - p.cu_k[b]);
   const int nsplit = k_len > 0 ? (k_len + p.chunk_tokens - 1) / p.chunk_tokens : 1;
-  if (nsplit <= 1) return;
+  // the decode grid wrote no partials for these (and reported them)
+  if (nsplit <= 1 || k_len > p.max_k || (int64_t)q0 >= p.num_q_rows) return;
   const int64_t base = (int64_t)b * p.max_splits * p.num_q_heads + hq;
   float mx = -INFINITY;
   for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.ws_lse[base + (int64_t)s * p.num_q_heads]);
@@ -324,6 +324,7 @@ int launch_paged_decode(const AttnArgs& a) {
   p.page_size = a.page;
   p.chunk_tokens = chunk;
   p.max_k = a.max_k;
+  p.num_q_rows = a.num_q_rows;
   p.max_splits = splits;
   p.scale_log2 = a.scale * kLog2e;
   p.ws_o = nullptr;
@@ -334,11 +335,7 @@ int launch_paged_decode(const AttnArgs& a) {
     p.ws_o = reinterpret_cast<float*>(a.ws);
     p.ws_lse = p.ws_o + n * kDecD;
   }
-#ifdef NVKV_DECODE_SPLIT_MAJOR
-  dim3 grid(a.num_seqs, a.hkv, splits);
-#else
   dim3 grid(splits, a.hkv, a.num_seqs);
-#endif
   // group sizes up to 8 leave fragment rows 8..15 as padding (kHi = false)
   const bool hi = p.group > 8;
   if (a.dtype == NVKV_DTYPE_BF16) {

@@ -103,6 +103,8 @@ struct PrefillParams {
   const uint4* plan_seq;
   const uint32_t* plan_b;
   int num_seqs;
+  int max_k;           // max_seqlen_k: the block tables cover this many keys
+  int64_t num_q_rows;  // rows of q and out
   int causal;
   float scale_log2;
   int* err;
@@ -348,13 +350,17 @@ __device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t p_tmem, ui
 }
 
 // ---- work plan --------------------------------------------------------------
-// q tiles of sequence b (0: a decode row, q_len <= 1).  With `err`, records
-// k_len < q_len (then 0) and q_len > max_seqlen_q (clamped to num_q_tiles).
-__device__ __forceinline__ int pf_seq_tiles(const uint32_t* cu_q, const uint32_t* cu_k, int b,
-                                            int num_q_tiles, int* err) {
-  const int q_len = (int)(cu_q[b + 1] - cu_q[b]);
+// Checks one sequence's lengths against the buffers before anything is read
+// or written for it.  Returns its q tiles, 0 for a decode row (q_len <= 1,
+// the decode kernel's) and 0 for a malformed sequence: k_len < q_len, k_len
+// > max_seqlen_k (its block-table row covers only max_seqlen_k keys) or rows
+// qs .. qs + q_len past the q/out buffers.  q_len > max_seqlen_q is clamped
+// to num_q_tiles.  With `err`, every malformed case is recorded as
+// NVKV_DEVERR_SEQLEN.
+__device__ __forceinline__ int pf_check_seq(uint32_t qs, int q_len, int k_len, int num_q_tiles,
+                                            int max_k, int64_t num_q_rows, int* err) {
   if (q_len <= 1) return 0;
-  if ((int)(cu_k[b + 1] - cu_k[b]) < q_len) {
+  if (k_len < q_len || k_len > max_k || (int64_t)qs + q_len > num_q_rows) {
     if (err) record_error(err, NVKV_DEVERR_SEQLEN);
     return 0;
   }
@@ -364,6 +370,13 @@ __device__ __forceinline__ int pf_seq_tiles(const uint32_t* cu_q, const uint32_t
     return num_q_tiles;
   }
   return n;
+}
+__device__ __forceinline__ int pf_seq_tiles(const uint32_t* cu_q, const uint32_t* cu_k, int b,
+                                            int num_q_tiles, int max_k, int64_t num_q_rows,
+                                            int* err) {
+  const uint32_t qs = cu_q[b];
+  return pf_check_seq(qs, (int)(cu_q[b + 1] - qs), (int)(cu_k[b + 1] - cu_k[b]), num_q_tiles,
+                      max_k, num_q_rows, err);
 }
 
 // Block-wide exclusive scan over 1024 threads; *total gets the sum.
@@ -405,7 +418,8 @@ __host__ __device__ inline size_t pf_plan_seq_word(int num_q_tiles) {
 
 __global__ void __launch_bounds__(1024)
     prefill_plan_kernel(const uint32_t* cu_q, const uint32_t* cu_k, int num_seqs,
-                        int num_q_tiles, uint32_t* plan, int* err) {
+                        int num_q_tiles, int max_k, int64_t num_q_rows, uint32_t* plan,
+                        int* err) {
   pdl_launch_dependents();  // the prefill grid may start its prologue now
   extern __shared__ uint32_t hist[];  // [num_q_tiles + 1]: sequences per count, then cursors
   __shared__ uint32_t part[32], total, tiles;
@@ -414,7 +428,7 @@ __global__ void __launch_bounds__(1024)
   if (tid == 0) tiles = 0;
   __syncthreads();
   for (int b = tid; b < num_seqs; b += 1024) {
-    const int n = pf_seq_tiles(cu_q, cu_k, b, Q, err);
+    const int n = pf_seq_tiles(cu_q, cu_k, b, Q, max_k, num_q_rows, err);
     if (n > 0) {
       atomicAdd(&hist[n], 1u);
       atomicAdd(&tiles, (uint32_t)n);
@@ -441,7 +455,7 @@ __global__ void __launch_bounds__(1024)
   uint4* seq = reinterpret_cast<uint4*>(plan + pf_plan_seq_word(Q));
   uint32_t* ids = reinterpret_cast<uint32_t*>(seq + num_seqs);
   for (int b = tid; b < num_seqs; b += 1024) {
-    const int n = pf_seq_tiles(cu_q, cu_k, b, Q, nullptr);
+    const int n = pf_seq_tiles(cu_q, cu_k, b, Q, max_k, num_q_rows, nullptr);
     if (n > 0) {
       const uint32_t pos = atomicAdd(&hist[n], 1u);
       const uint32_t qs = cu_q[b], ks = cu_k[b];
@@ -467,8 +481,8 @@ __device__ __forceinline__ int pf_num_items(const PrefillParams& p) {
                : p.num_q_tiles * p.num_head_slots * p.num_seqs;
 }
 // Direct enumeration: the same level order with every sequence in each level;
-// returns false for an empty item (a decode row, a tile past q_len, or a bad
-// sequence, which is then reported).
+// returns false for an empty item (a decode row, a tile past q_len, or a
+// malformed sequence, which pf_check_seq reports).
 __device__ __forceinline__ bool pf_item_direct(const PrefillParams& p, int w, PfItem& it) {
   const int per_tile = p.num_head_slots * p.num_seqs;
   const int qt = p.num_q_tiles - 1 - w / per_tile;
@@ -484,10 +498,11 @@ __device__ __forceinline__ bool pf_item_direct(const PrefillParams& p, int w, Pf
   it.ks = __ldg(p.cu_k + it.b);
   it.k_len = (int)(__ldg(p.cu_k + it.b + 1) - it.ks);
   it.off = it.k_len - it.q_len;
-  if (it.off < 0 || (qt == p.num_q_tiles - 1 && it.q_len > p.num_q_tiles * kPfBM)) {
-    record_error(p.err, NVKV_DEVERR_SEQLEN);
-    if (it.off < 0) return false;
-  }
+  // every item of a sequence is checked; the items of q tile 0 (which every
+  // prompt has) report, once per head slot
+  if (pf_check_seq(it.qs, it.q_len, it.k_len, p.num_q_tiles, p.max_k, p.num_q_rows,
+                   qt == 0 ? p.err : nullptr) == 0)
+    return false;
   const int last_row = min(it.i0 + kPfBM, it.q_len) - 1;
   const int kmax = p.causal ? min(it.k_len, last_row + it.off + 1) : it.k_len;
   it.ntiles = (kmax + kPfBN - 1) / kPfBN;
@@ -896,12 +911,14 @@ int launch_paged_prefill(const AttnArgs& a) {
                         : nullptr;
   p.plan_b = use_plan ? reinterpret_cast<const uint32_t*>(p.plan_seq + a.num_seqs) : nullptr;
   p.num_seqs = a.num_seqs;
+  p.max_k = a.max_k;
+  p.num_q_rows = a.num_q_rows;
   p.causal = a.causal;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.err = device_error_word();
   if (use_plan) {
     prefill_plan_kernel<<<1, 1024, (p.num_q_tiles + 1) * sizeof(uint32_t), a.stream>>>(
-        a.cu_q, a.cu_k, a.num_seqs, p.num_q_tiles, plan, p.err);
+        a.cu_q, a.cu_k, a.num_seqs, p.num_q_tiles, a.max_k, a.num_q_rows, plan, p.err);
     rc = check_cuda(cudaGetLastError(), "prefill plan launch");
     if (rc) return rc;
   }

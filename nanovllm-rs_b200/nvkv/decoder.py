@@ -32,30 +32,9 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
+from qwen3_config import QWEN3_0_6B, QWEN3_4B, QWEN3_8B, QWEN3_32B, Qwen3Config  # noqa: F401
+
 from . import ops
-
-
-@dataclass
-class Qwen3Config:
-    """The config.json fields the reference reads (config.rs:5-27)."""
-
-    hidden_size: int
-    num_hidden_layers: int
-    num_attention_heads: int
-    num_key_value_heads: int
-    intermediate_size: int
-    vocab_size: int = 151936
-    head_dim: int = 128
-    rms_norm_eps: float = 1e-6
-    rope_theta: float = 1e6
-    max_position_embeddings: int = 40960
-    tie_word_embeddings: bool = False
-
-
-QWEN3_0_6B = Qwen3Config(1024, 28, 16, 8, 3072, tie_word_embeddings=True)
-QWEN3_4B = Qwen3Config(2560, 36, 32, 8, 9728, tie_word_embeddings=True)
-QWEN3_8B = Qwen3Config(4096, 36, 32, 8, 12288)
-QWEN3_32B = Qwen3Config(5120, 64, 64, 8, 25600)
 
 
 # ---------------------------------------------------------------------------
@@ -258,7 +237,7 @@ class Qwen3TP:
     def forward(self, st: Step) -> torch.Tensor:
         """Qwen3ForCausalLM::forward + compute_logits (qwen3.rs:285-297,
         embed_head.rs:89-119): returns the full-vocab logits of each
-        sequence's last token, [B, V] (float32)."""
+        sequence's last token, [B, V], in the model dtype."""
         return gather_logits(self._local_logits(st), self.group)
 
     @torch.no_grad()
@@ -268,7 +247,7 @@ class Qwen3TP:
         return vocab_parallel_argmax(self._local_logits(st), self.rank, self.group)
 
     def _local_logits(self, st: Step) -> torch.Tensor:
-        """This rank's vocab shard of the last-token logits, [B, V/tp] float32."""
+        """This rank's vocab shard of the last-token logits, [B, V/tp], model dtype."""
         if self.comm is not None:
             return self._local_logits_peer(st)
         cfg = self.cfg
@@ -306,9 +285,9 @@ class Qwen3TP:
             h = self._all_reduce(torch.matmul(act, L["down"].t()))
         h = ops.rms_norm(h, self.norm, eps, residual=residual, out=xb)  # qwen3.rs:295
         last = h.index_select(0, st.last_idx)
-        # bf16 operands, fp32 output: no bf16 rounding of the logits, so the
-        # greedy argmax sees no artificial ties
-        return torch.mm(last, self.lm_head.t(), out_dtype=torch.float32)
+        # logits in the model dtype, as the reference's lm_head matmul gives
+        # them (embed_head.rs:113); its sampler widens them to f32 afterwards
+        return torch.mm(last, self.lm_head.t())
 
     def _local_logits_peer(self, st: Step) -> torch.Tensor:
         """_local_logits with every all-reduce fused into the RMSNorm after it:
@@ -354,7 +333,7 @@ class Qwen3TP:
             nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.norm
             self.comm.allreduce_rms_norm(T, H, res, nxt, eps, xb)
         last = xb.index_select(0, st.last_idx)
-        return torch.mm(last, self.lm_head.t(), out_dtype=torch.float32)
+        return torch.mm(last, self.lm_head.t())
 
     def launches_per_step(self, st: Step) -> int:
         """nvkv kernel launches one forward issues: per layer two RMSNorms

@@ -213,17 +213,17 @@ def prepare_model_input(seqs: Seq_[Seq], block_size: int) -> Tuple[np.ndarray, n
 
 
 def gather_paged_kv(k_cache, v_cache, block_table_row, seqlen_k: int, page_size: int):
-    """layers/attention.rs:143-164: token-ordered rows of one sequence."""
-    slots: List[int] = []
-    for b in block_table_row:
-        for s in range(page_size):
-            if len(slots) == seqlen_k:
-                break
-            slots.append(int(b) * page_size + s)
-        if len(slots) == seqlen_k:
-            break
+    """layers/attention.rs:143-164: token-ordered rows of one sequence.
+
+    The reference walks the block-table row page by page, pushing
+    ``block * page_size + s`` for s = 0..page_size until it holds seqlen_k
+    slots (fewer if the row runs out); the same list is formed here as one
+    array, ``(row[:, None] * page_size + arange(page_size)).ravel()[:seqlen_k]``.
+    """
+    row = np.asarray(block_table_row, dtype=np.int64).reshape(-1)
+    slots = (row[:, None] * page_size + np.arange(page_size, dtype=np.int64)).reshape(-1)
+    idx = slots[:seqlen_k]
     hkv, d = k_cache.shape[2], k_cache.shape[3]
-    idx = np.asarray(slots, dtype=np.int64)
     return k_cache.reshape(-1, hkv, d)[idx], v_cache.reshape(-1, hkv, d)[idx]
 
 
@@ -240,9 +240,9 @@ def causal_attention_one(q, k, v, scale: float, causal: bool = True, acc=np.floa
     if q_len == 0:
         return np.zeros((0, hq, d), np.float32)
     g = hq // hkv
-    qh = q.astype(acc).reshape(q_len, hkv, g, d).transpose(1, 2, 0, 3)  # [hkv,g,q,d]
-    kh = k.astype(acc).transpose(1, 2, 0)  # [hkv,d,k]
-    vh = v.astype(acc).transpose(1, 0, 2)  # [hkv,k,d]
+    qh = q.astype(acc, copy=False).reshape(q_len, hkv, g, d).transpose(1, 2, 0, 3)  # [hkv,g,q,d]
+    kh = k.astype(acc, copy=False).transpose(1, 2, 0)  # [hkv,d,k]
+    vh = v.astype(acc, copy=False).transpose(1, 0, 2)  # [hkv,k,d]
     s = np.matmul(qh, kh[:, None]) * scale  # [hkv,g,q,k]
     if causal:
         i = np.arange(q_len)[:, None]
@@ -267,27 +267,40 @@ def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, causal=True, ac
 
 
 def paged_attention(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables, scale,
-                    causal=True, acc=np.float64):
+                    causal=True, acc=np.float64, pool=None):
     """Paged route (layers/attention.rs:38-59) computed the fallback way
-    (attention.rs:105-136): gather each sequence's rows, then attend."""
+    (attention.rs:105-136): gather each sequence's rows, then attend.
+
+    ``pool`` (a concurrent.futures executor) runs the independent
+    per-sequence gathers and attentions on several host threads; the result
+    is the same as the serial loop."""
     out = np.zeros(q.shape, np.float32)
     page = k_cache.shape[1]
-    for b in range(len(cu_seqlens_q) - 1):
+
+    def one(b):
         q0, q1 = int(cu_seqlens_q[b]), int(cu_seqlens_q[b + 1])
         k_len = int(cu_seqlens_k[b + 1]) - int(cu_seqlens_k[b])
         kb, vb = gather_paged_kv(k_cache, v_cache, block_tables[b], k_len, page)
         out[q0:q1] = causal_attention_one(q[q0:q1], kb, vb, scale, causal, acc)
+
+    seqs = range(len(cu_seqlens_q) - 1)
+    if pool is None:
+        for b in seqs:
+            one(b)
+    else:
+        list(pool.map(one, seqs))
     return out
 
 
-def attention_forward(q, k, v, ctx: Context, k_cache, v_cache, scale, acc=np.float64):
+def attention_forward(q, k, v, ctx: Context, k_cache, v_cache, scale, acc=np.float64,
+                      pool=None):
     """Attention::forward (layers/attention.rs:85-137): store, then attend
     through the block table when present, else on the fresh K/V."""
     if k_cache is not None and v_cache is not None:
         store_kvcache(k, v, k_cache, v_cache, ctx.slot_mapping)
     if ctx.block_tables is not None:
         return paged_attention(q, k_cache, v_cache, ctx.cu_seqlens_q, ctx.cu_seqlens_k,
-                               ctx.block_tables, scale, True, acc)
+                               ctx.block_tables, scale, True, acc, pool)
     return varlen_attention(q, k, v, ctx.cu_seqlens_q, ctx.cu_seqlens_k, scale, True, acc)
 
 

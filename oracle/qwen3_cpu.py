@@ -28,14 +28,16 @@ class Qwen3CPU:
                  dtype: str = "f32"):
         """dtype 'f32' is config 1's fp32 CPU route; 'bf16' rounds to bf16 at
         every op boundary of the reference's candle bf16 route (GEMM outputs,
-        norms, RoPE, attention output, SiLU*mul, residual adds) with f32
-        arithmetic inside each op; logits stay f32."""
+        norms, RoPE, attention output, SiLU*mul, residual adds, and the
+        lm_head logits, embed_head.rs:113) with f32 arithmetic inside each
+        op."""
         self.cfg, self.w, self.dt = cfg, weights, dtype
         D = cfg.head_dim
         self.P = block_size
         shape = (num_blocks, block_size, cfg.num_key_value_heads, D)
         self.k = [np.zeros(shape, np.float32) for _ in range(cfg.num_hidden_layers)]
         self.v = [np.zeros(shape, np.float32) for _ in range(cfg.num_hidden_layers)]
+        self.pool = None  # optional executor: per-sequence attention on host threads
 
     def _mm(self, x, w):
         return O.round_to(x @ w.T, self.dt)
@@ -51,7 +53,8 @@ class Qwen3CPU:
         q, k, v = O.qknorm_rope(qkv, positions, Hq, Hkv, D, w[f"{i}.qn"], w[f"{i}.kn"],
                                 c.rms_norm_eps, c.rope_theta, dt)
         o = O.round_to(O.attention_forward(q, k, v, ctx, self.k[i], self.v[i], D ** -0.5,
-                                           acc=np.float32 if dt == "f32" else np.float64), dt)
+                                           acc=np.float32 if dt == "f32" else np.float64,
+                                           pool=self.pool), dt)
         a = self._mm(o.reshape(len(q), -1), w[f"{i}.o"])
         x, residual = O.residual_rms_norm(a, residual, w[f"{i}.ln2"], c.rms_norm_eps, dt)
         act = O.silu_and_mul(self._mm(x, w[f"{i}.gate_up"]), dt)
@@ -68,7 +71,7 @@ class Qwen3CPU:
         last = ctx.cu_seqlens_q[1:].astype(np.int64) - 1
         if len(ctx.seq_need_compute_logits):
             last = last[ctx.seq_need_compute_logits]
-        return h[last] @ w["lm_head"].T
+        return O.round_to(h[last] @ w["lm_head"].T, self.dt)
 
 
 def advance(seqs: List[O.Seq], tokens, free_blocks: List[int], P: int) -> None:

@@ -243,3 +243,30 @@ def test_decode_context_above_max_seqlen_is_reported():
     assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
     kb, vb = gather_seq(kc, vc, tables[1], 200)
     assert_attention_close(out[1:2], O.causal_attention_one(f32(q)[1:2], kb, vb, 0.1), "row 1")
+
+
+def test_decode_rows_past_num_q_tokens_are_skipped():
+    """cu_seqlens_q pointing past num_q_tokens (a caller bug): the q and out
+    buffers are over-allocated, the call is given only the first rows, and
+    the row the metadata places beyond them must be neither computed nor
+    written (its out row keeps a canary) while DEVERR_SEQLEN is reported.
+    Once with a split-KV plan (long contexts) and once without."""
+    for lens, seed in (([300, 2000, 5000], 32), ([100, 90, 80], 33)):
+        g = torch.Generator().manual_seed(seed)
+        B = len(lens)
+        nb = sum((L + 255) // 256 for L in lens) + 1
+        kc, vc, bt, tables = make_paged(lens, 256, 2, 128, nb, g)
+        q_all = torch.randn(B, 8, 128, generator=g).to(torch.bfloat16).cuda()
+        out_all = torch.full((B, 8, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+        nvkv.device_error()
+        nvkv.paged_attention(q_all[:B - 1], kc, vc, cu([1] * B), cu(lens),
+                             torch.from_numpy(bt.view(np.int32)).cuda(), 1, max(lens), 0.1,
+                             out=out_all[:B - 1])
+        torch.cuda.synchronize()
+        assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
+        assert bool((out_all[B - 1] == 7.0).all()), "row past num_q_tokens was written"
+        for b in range(B - 1):
+            kb, vb = gather_seq(kc, vc, tables[b], lens[b])
+            assert_attention_close(out_all[b:b + 1],
+                                   O.causal_attention_one(f32(q_all)[b:b + 1], kb, vb, 0.1),
+                                   f"row {b}")

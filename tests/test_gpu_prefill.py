@@ -168,3 +168,54 @@ def test_work_plan_bad_lengths_reported():
         want = O.causal_attention_one(f32(q)[c[good]:c[good + 1]], f32(k)[ck[good]:ck[good + 1]],
                                       f32(v)[ck[good]:ck[good + 1]], d ** -0.5, True)
         assert_attention_close(out[c[good]:c[good + 1]], want, "the well-formed prompt")
+
+
+def _bounds_case(q_lens, k_lens, given_rows, max_q, max_k, hq, hkv, bad, seed):
+    """Paged prompts whose metadata is wrong for sequence `bad`, on buffers
+    large enough that a kernel ignoring the checks would stay in bounds: q and
+    out hold sum(q_lens) rows, but only `given_rows` are passed; the block
+    tables are wide enough for every k_len.  Sequence `bad` must leave its
+    out rows untouched (canary) and DEVERR_SEQLEN must be reported; every
+    other sequence must match the oracle."""
+    g = torch.Generator().manual_seed(seed)
+    d, P = 128, 256
+    nb = sum((k + P - 1) // P for k in k_lens) + 1
+    kc, vc, bt, tables = make_paged(k_lens, P, hkv, d, nb, g)
+    T = sum(q_lens)
+    q_all = torch.randn(T, hq, d, generator=g).to(torch.bfloat16).cuda()
+    out_all = torch.full((T, hq, d), 7.0, dtype=torch.bfloat16, device="cuda")
+    nvkv.device_error()
+    nvkv.paged_attention(q_all[:given_rows], kc, vc, cu(q_lens), cu(k_lens),
+                         torch.from_numpy(bt.view(np.int32)).cuda(), max_q, max_k, d ** -0.5,
+                         out=out_all[:given_rows])
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == nvkv._lib.DEVERR_SEQLEN
+    c = np.cumsum([0] + list(q_lens))
+    assert bool((out_all[c[bad]:c[bad + 1]] == 7.0).all()), "a skipped sequence was written"
+    qn = f32(q_all)
+    for b in range(len(q_lens)):
+        if b == bad:
+            continue
+        kb, vb = gather_seq(kc, vc, tables[b], k_lens[b])
+        want = O.causal_attention_one(qn[c[b]:c[b + 1]], kb, vb, d ** -0.5, True)
+        assert_attention_close(out_all[c[b]:c[b + 1]], want, f"sequence {b}")
+
+
+@pytest.mark.parametrize("decodes", [0, 400])
+def test_prefill_k_len_above_max_seqlen_k_is_skipped(decodes):
+    """k_len > max_seqlen_k on a prompt: its block-table row only has to
+    cover max_seqlen_k keys, so the kernel must not walk it (direct
+    enumeration without decode rows; the work plan with 400 of them)."""
+    q_lens = [1] * decodes + [300, 200]
+    k_lens = [5] * decodes + [300, 700]
+    _bounds_case(q_lens, k_lens, sum(q_lens), 300, 600, 8, 2, decodes + 1, seed=60 + decodes)
+
+
+@pytest.mark.parametrize("decodes", [0, 400])
+def test_prefill_rows_past_num_q_tokens_are_skipped(decodes):
+    """A prompt whose query rows reach past num_q_tokens: nothing of it is
+    computed or written (direct enumeration, and the work plan)."""
+    q_lens = [1] * decodes + [300, 200]
+    k_lens = [5] * decodes + [300, 450]
+    _bounds_case(q_lens, k_lens, sum(q_lens) - 50, 300, 450, 8, 2, decodes + 1,
+                 seed=70 + decodes)

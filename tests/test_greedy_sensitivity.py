@@ -7,7 +7,7 @@ import numpy as np
 
 import nvkv_oracle as O
 import qwen3_cpu as Q
-from nvkv.decoder import Qwen3Config
+from qwen3_config import Qwen3Config
 
 CFG = Qwen3Config(256, 2, 4, 2, 512, vocab_size=2000)
 P = 256

@@ -161,3 +161,49 @@ def test_rope_and_norm_rounding_points():
     # position 0: RoPE is the identity, so q == rms_norm(q)
     qn = O.rms_norm(qkv[0, :hq * d].reshape(hq, d), w, 1e-6, "bf16")
     assert np.array_equal(q16[0], qn)
+
+
+def _gather_loop(k_cache, v_cache, row, seqlen_k, page):
+    """attention.rs:148-163 as the reference writes it: push block*page + s
+    page by page, stop at seqlen_k slots."""
+    slots = []
+    for b in row:
+        for s in range(page):
+            if len(slots) == seqlen_k:
+                break
+            slots.append(int(b) * page + s)
+        if len(slots) == seqlen_k:
+            break
+    hkv, d = k_cache.shape[2], k_cache.shape[3]
+    idx = np.asarray(slots, dtype=np.int64)
+    return k_cache.reshape(-1, hkv, d)[idx], v_cache.reshape(-1, hkv, d)[idx]
+
+
+def test_gather_paged_kv_equals_the_slot_loop():
+    """The oracle's array form of gather_paged_kv gives exactly the rows of
+    the reference's slot loop: partial last pages, whole pages, a row with
+    more pages than needed, and a row with fewer (the loop then stops short)."""
+    rng = np.random.default_rng(5)
+    P, nb = 16, 12
+    kc = rng.standard_normal((nb, P, 2, 4)).astype(np.float32)
+    vc = rng.standard_normal((nb, P, 2, 4)).astype(np.float32)
+    for row, L in (([3, 7, 1], 40), ([3, 7, 1], 48), ([5, 2, 9, 0], 17), ([4], 16), ([4, 6], 50),
+                   ([8], 0)):
+        got = O.gather_paged_kv(kc, vc, np.asarray(row), L, P)
+        want = _gather_loop(kc, vc, row, L, P)
+        assert got[0].shape == want[0].shape and np.array_equal(got[0], want[0])
+        assert np.array_equal(got[1], want[1])
+
+
+def test_reference_arm_imports_no_native_library():
+    """bench.py's CPU arm (the oracle restatement and the shapes it runs)
+    must not load libnvkv.so: importing bench, the config module and the
+    oracle leaves the nvkv package unimported."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]; import bench, qwen3_config, nvkv_oracle, "
+            "qwen3_cpu; bad = [m for m in sys.modules if m == 'nvkv' or m.startswith('nvkv.')]; "
+            "assert not bad, bad" % (root, os.path.join(root, "nanovllm-rs_b200"),
+                                     os.path.join(root, "oracle")))
+    subprocess.run([sys.executable, "-c", code], check=True, cwd=root)
