@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--nccl-allreduce", action="store_true",
                     help="tp > 1: NCCL all-reduce + nvkv_rms_norm instead of the fused "
                          "peer-memory nvkv_allreduce_rms_norm")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the whole-workload runs (configs 4, 3, 1, 5) after the timed step")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -271,6 +273,354 @@ def _peer_allreduce_bw(model, world, dev, T, reps=50):
     return ms, algbw, algbw * 2 * (world - 1) / world
 
 
+def _bf16_ulps(a, b):
+    """Largest distance between two bf16 tensors in units in the last place
+    (sign-magnitude bit patterns mapped onto one ordered integer line)."""
+    import torch
+
+    def line(t):
+        i = t.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+
+    return int((line(a) - line(b)).abs().max()) if a.numel() else 0
+
+
+def tp_parity(cfg, comm, world, rank, dev, T=NUM_SEQS, layers=4, num_seqs=4, steps=12, seed=17,
+              dtype=None):
+    """Correctness of the tensor-parallel step on this run's own ranks, before
+    its numbers are trusted.  Every rank takes the same collective calls.
+
+    * allreduce_vs_nccl: the step's fused all-reduce + residual + RMSNorm
+      (nvkv_allreduce_rms_norm through `comm`, when the step uses it; comm
+      None is the NCCL route) against NCCL's
+      all-reduce followed by nvkv_rms_norm on the same [T, hidden] inputs;
+      bit-identical at TP2 (one rounding of a two-term sum on both routes),
+      within one bf16 ulp of the sum at TP4/8 (NCCL's ring rounds per hop).
+    * greedy_vs_tp1: a `layers`-layer slice of the same Qwen3 shape built at
+      TP=N (sharded over the ranks, the step's all-reduce route) and at TP=1
+      (every rank builds the whole slice from the same seeds), `num_seqs`
+      prompts of U[32, 64] random tokens, one prefill step then greedy decode
+      steps, teacher forced with the TP=1 tokens; the TP=N greedy token must
+      equal TP=1's at >= 95 % of positions (the north star's bar), and the
+      prefill logits' max-abs difference is reported.
+    Step metadata comes from nvkv's own prepare_step (the C ABI)."""
+    import torch
+    import torch.distributed as dist
+    from dataclasses import replace
+
+    from nvkv import ops
+    from nvkv.blocks import Sequence, prepare_step
+    from nvkv.decoder import Qwen3TP, Step
+
+    dtype = dtype or torch.bfloat16
+    res = {}
+    eps = cfg.rms_norm_eps
+    H = cfg.hidden_size
+    if comm is not None:
+        g = torch.Generator(device=dev).manual_seed(1000 + rank)
+        x = torch.randn(T, H, generator=g, device=dev).to(dtype)
+        g0 = torch.Generator(device=dev).manual_seed(999)  # replicated: residual, weight
+        r0 = torch.randn(T, H, generator=g0, device=dev).to(dtype)
+        wn = (1 + 0.1 * torch.randn(H, generator=g0, device=dev)).to(dtype)
+        comm.input(T, H, dtype).copy_(x)
+        res_a, out_a = r0.clone(), torch.empty_like(r0)
+        comm.allreduce_rms_norm(T, H, res_a, wn, eps, out_a)
+        xs = x.clone()
+        dist.all_reduce(xs)
+        res_b = r0.clone()
+        out_b = ops.rms_norm(xs, wn, eps, residual=res_b)
+        torch.cuda.synchronize()
+        stats = torch.tensor([_bf16_ulps(res_a, res_b), _bf16_ulps(out_a, out_b),
+                              float((out_a.float() - out_b.float()).abs().max())],
+                             dtype=torch.float64, device=dev)
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        su, ou, od = [float(v) for v in stats.tolist()]
+        ok = (su == 0 and ou == 0) if world == 2 else su <= 1 and od <= 2e-2
+        res["allreduce_vs_nccl"] = {
+            "shape": [T, H], "sum_max_ulps": int(su), "out_max_ulps": int(ou),
+            "out_max_abs": od, "bar": "bitwise" if world == 2 else "sum <= 1 ulp, out <= 2e-2",
+            "ok": bool(ok)}
+    cfg = replace(cfg, num_hidden_layers=layers)
+    kw = dict(seed=seed, device=dev, embed_std=0.05, head_std=1.0, dtype=dtype)
+    m_n = Qwen3TP(cfg, rank, world, comm=comm, peer_allreduce=comm is not None, max_tokens=T,
+                  **kw)
+    m_1 = Qwen3TP(cfg, 0, 1, **kw)
+    P = PAGE
+    rng = np.random.default_rng(seed)
+    seqs = [Sequence(rng.integers(0, cfg.vocab_size, int(L)).tolist(), P)
+            for L in rng.integers(32, 65, num_seqs)]
+    for i, sq in enumerate(seqs):
+        sq.block_table = [i]  # one page holds prompt + steps (<= 64 + 12 tokens)
+    for m in (m_n, m_1):
+        m.allocate_kv_cache(num_seqs, P)
+    agree, total, logit_diff = 0, 0, 0.0
+    for step in range(steps):
+        for sq in seqs:
+            sq.num_new_tokens = len(sq) - sq.num_cached_tokens
+        meta = prepare_step(seqs, P)
+        bt = np.asarray([sq.block_table for sq in seqs], np.int32)
+        t = lambda a, dt=None: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+        cu_q = t(meta["cu_seqlens_q"].view(np.int32))
+        st = Step(t(meta["input_ids"]), t(meta["positions"]), t(meta["slot_mapping"]), cu_q,
+                  t(meta["cu_seqlens_k"].view(np.int32)), t(bt), (cu_q[1:] - 1).long(),
+                  meta["max_seqlen_q"], meta["max_seqlen_k"])
+        if step == 0:
+            ln, l1 = m_n.forward(st), m_1.forward(st)
+            logit_diff = float((ln.float() - l1.float()).abs().max())
+            tok_n, tok_1 = ln.argmax(-1), l1.argmax(-1)
+        else:
+            tok_n, tok_1 = m_n.greedy(st), m_1.greedy(st)
+        agree += int((tok_n == tok_1).sum())
+        total += num_seqs
+        for sq, tk in zip(seqs, tok_1.tolist()):  # teacher forced: the TP=1 token
+            sq.num_cached_tokens += sq.num_new_tokens
+            sq.num_new_tokens = 0
+            sq.append_token(tk)
+    torch.cuda.synchronize()
+    stats = torch.tensor([-agree / total, logit_diff], dtype=torch.float64, device=dev)
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)  # worst rank
+    frac = -float(stats[0])
+    res["greedy_vs_tp1"] = {"layers": layers, "seqs": num_seqs, "positions": total,
+                            "agree": round(frac, 4), "prefill_logits_max_abs": float(stats[1]),
+                            "bar": ">= 0.95 of positions", "ok": frac >= 0.95}
+    res["ok"] = all(v["ok"] for v in res.values() if isinstance(v, dict))
+    m_n.close()
+    del m_n, m_1
+    torch.cuda.empty_cache()
+    return res
+
+
+MAX_BATCHED = 16384  # EngineConfig default max_num_batched_tokens (config.rs:110-120)
+
+
+def _timing_max(summary, world, dev):
+    """Worst rank's host times, and the rates recomputed from them."""
+    for k in ("prefill_s", "decode_s", "total_s"):
+        summary[k] = round(_max_over_ranks(summary[k], world, dev), 4)
+    summary["prompt_tok_s"] = round(summary["prompt_tokens"] / max(summary["prefill_s"], 1e-9), 1)
+    summary["decode_tok_s"] = round(summary["decode_tokens"] / max(summary["decode_s"], 1e-9), 1)
+    summary["output_tok_s"] = round(summary["generated_tokens"] / max(summary["total_s"], 1e-9), 1)
+    return summary
+
+
+def run_workload(model, world, dev, prompts, max_tokens, num_blocks, warm_prompts=None):
+    """Every prompt to completion through nvkv.engine (the reference's engine
+    loop and scheduler defaults, greedy), on a fresh KV pool of `num_blocks`
+    pages; host-clock step times (schedule + metadata + H2D + model + D2H of
+    the tokens), worst rank.  `warm_prompts` run first, untimed, so library
+    warm-up (cuBLAS heuristics for the step shapes) stays out of the timing."""
+    import torch
+
+    from nvkv.engine import Engine
+
+    model.k_caches, model.v_caches = [], []
+    torch.cuda.empty_cache()
+    model.allocate_kv_cache(num_blocks, PAGE)
+    if warm_prompts:
+        eng = Engine(model, num_blocks, PAGE, max_num_batched_tokens=MAX_BATCHED)
+        eng.generate(warm_prompts, 2)
+        eng.close()
+    eng = Engine(model, num_blocks, PAGE, max_num_batched_tokens=MAX_BATCHED)
+    _barrier(world)
+    outs = eng.generate(prompts, max_tokens)
+    torch.cuda.synchronize()
+    summary = _timing_max(eng.summary(), world, dev)
+    eng.close()
+    summary["kv_pool_blocks"] = num_blocks
+    model.k_caches, model.v_caches = [], []
+    torch.cuda.empty_cache()
+    return summary, outs
+
+
+def workload_config4(model, world, dev):
+    """BASELINE config 4 end to end: 256 requests x 1024-token prompts of
+    uniform random ids, 512 greedy tokens each, P=256, every step through the
+    engine loop (prefill and mixed steps at the 16384-token budget, then
+    decode)."""
+    rng = np.random.default_rng(41)
+    V = model.cfg.vocab_size
+    prompts = [rng.integers(0, V, PROMPT).tolist() for _ in range(NUM_SEQS)]
+    warm = [rng.integers(0, V, PROMPT).tolist() for _ in range(MAX_BATCHED // PROMPT)]
+    need = NUM_SEQS * ((PROMPT + MAX_OUT + PAGE - 1) // PAGE) + 16
+    s, _ = run_workload(model, world, dev, prompts, MAX_OUT, need, warm)
+    s["workload"] = ("config 4: Qwen3-8B, 256 requests x 1024-token prompts, 512 greedy tokens "
+                     "each, P=256, max_num_batched_tokens 16384, chunked prefill off")
+    return s
+
+
+def workload_config3(world, rank, dev, comm):
+    """Qwen3-4B (random-init bf16), 128 requests with
+    prompts U[128, 2048] of uniform random ids, 256 greedy tokens each,
+    continuous batching with mixed prefill/decode steps."""
+    import torch
+
+    from nvkv.decoder import QWEN3_4B, Qwen3TP
+    m = Qwen3TP(QWEN3_4B, rank, world, seed=4, device=dev, comm=comm,
+                peer_allreduce=comm is not None, max_tokens=MAX_BATCHED)
+    rng = np.random.default_rng(43)
+    lens = rng.integers(128, 2049, 128)
+    prompts = [rng.integers(0, QWEN3_4B.vocab_size, int(L)).tolist() for L in lens]
+    warm = [rng.integers(0, QWEN3_4B.vocab_size, 2048).tolist() for _ in range(8)]
+    need = int(sum((L + 256 + PAGE - 1) // PAGE for L in lens)) + 16
+    s, _ = run_workload(m, world, dev, prompts, 256, need, warm)
+    s["workload"] = ("config 3: Qwen3-4B, 128 requests, prompts U[128,2048], 256 greedy tokens "
+                     f"each, P=256, tp{world}, continuous batching (mixed steps)")
+    m.close()
+    del m
+    torch.cuda.empty_cache()
+    return s
+
+
+def workload_config1(dev, cpu=True):
+    """BASELINE config 1's workload: Qwen3-0.6B architecture (random-init),
+    4 sequences with prompts U[64, 256] of uniform random ids, 32 greedy
+    tokens each, P=256.  GPU: the nvkv path in bf16 through the engine loop
+    (host clock, end to end).  CPU (`cpu_baseline`): the reference's fp32
+    CPU route restated (oracle/qwen3_cpu.py) with the same weights, the same
+    loop (one prefill step, then decode steps), all host threads."""
+    import torch
+
+    from nvkv.decoder import QWEN3_0_6B, Qwen3TP
+    rng = np.random.default_rng(45)
+    lens = rng.integers(64, 257, 4)
+    prompts = [rng.integers(0, QWEN3_0_6B.vocab_size, int(L)).tolist() for L in lens]
+    m = Qwen3TP(QWEN3_0_6B, 0, 1, seed=1, device=dev)
+    s, outs = run_workload(m, 1, dev, prompts, 32, 16, prompts)
+    s["workload"] = ("config 1: Qwen3-0.6B, 4 sequences, prompts U[64,256], 32 greedy tokens "
+                     "each, P=256; GPU bf16")
+    if cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import nvkv_oracle as O
+        import qwen3_cpu as Q
+        cores = _all_host_threads()
+        f = lambda t: t.float().cpu().numpy()  # noqa: E731
+        wts = {"embed": f(m.embed), "norm": f(m.norm), "lm_head": f(m.lm_head)}
+        for i, L in enumerate(m.layers):
+            for k in ("qkv", "o", "gate_up", "down", "ln1", "ln2", "qn", "kn"):
+                wts[f"{i}.{k}"] = f(L[k])
+        nb = 16
+        free = list(range(nb))[::-1]
+        seqs = [O.Seq(list(p), [free.pop() for _ in range((len(p) + PAGE - 1) // PAGE)], 0,
+                      len(p), PAGE) for p in prompts]
+        cpu_model = Q.Qwen3CPU(QWEN3_0_6B, wts, nb, PAGE, "f32")
+        t0 = time.perf_counter()
+        ref = Q.greedy_generate(cpu_model, seqs, 32, free)
+        t = time.perf_counter() - t0
+        gen = 4 * 32
+        s["cpu_baseline"] = {
+            "value": round(gen / t, 3), "unit": "generated tok/s", "total_s": round(t, 3),
+            "cores": cores, "kind": "port",
+            "sample": "the whole config-1 workload (one prefill step + 31 decode steps, 4 "
+                      "sequences), numpy fp32 restatement of the reference's CPU route"}
+        s["gpu_vs_cpu_speedup"] = round(t / s["total_s"], 1)
+        s["greedy_agreement_gpu_bf16_vs_cpu_fp32"] = round(float(np.mean(
+            [a == b for u, v in zip(outs, ref) for a, b in zip(u, v)])), 4)
+    del m
+    torch.cuda.empty_cache()
+    return s
+
+
+def workload_config5(world, rank, dev, comm, steps=128):
+    """BASELINE config 5 at TP8: Qwen3-32B (random-init bf16), 64 sequences
+    whose 32768-token contexts are already in the KV cache (filled with
+    random values instead of a 2M-token prefill), then `steps` greedy decode
+    tokens each.  One decode step (device-side metadata via
+    nvkv_decode_advance, all 64 layers, lm_head, vocab-parallel argmax) is
+    captured in a CUDA graph and replayed `steps` times between CUDA events,
+    worst rank.  The per-layer decode attention (split-KV at 1 kv head per
+    GPU) is timed alone the same way for its roofline."""
+    import torch
+
+    from nvkv import ops
+    from nvkv.decoder import QWEN3_32B, Qwen3TP, Step
+    B, ctx0 = 64, 32768
+    m = Qwen3TP(QWEN3_32B, rank, world, seed=6, device=dev, comm=comm,
+                peer_allreduce=comm is not None, max_tokens=MAX_BATCHED)
+    per = (ctx0 + steps + PAGE - 1) // PAGE
+    nb = B * per
+    m.allocate_kv_cache(nb, PAGE, fill_random=True)
+    bt = torch.arange(nb, dtype=torch.int32, device=dev).view(B, per)
+    lens = torch.full((B,), ctx0, dtype=torch.int64, device=dev)
+    ids = torch.randint(0, QWEN3_32B.vocab_size, (B,), device=dev)
+    pos = torch.empty(B, dtype=torch.int64, device=dev)
+    slots = torch.empty_like(pos)
+    cu_q = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    cu_k = torch.empty_like(cu_q)
+    st = Step(ids, pos, slots, cu_q, cu_k, bt, torch.arange(B, device=dev), 1, ctx0 + steps)
+
+    def one():
+        ops.decode_advance(lens, bt, nb, PAGE, pos, slots, cu_q, cu_k)
+        ids.copy_(m.greedy(st))
+
+    lens0 = lens.clone()
+    one()  # warm-up (eager)
+    torch.cuda.synchronize()
+    s_ = torch.cuda.Stream()
+    s_.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s_):
+        one()
+    torch.cuda.current_stream().wait_stream(s_)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        one()
+    lens.copy_(lens0)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    g.reset()
+    # decode attention alone, one layer's call on the last step's metadata
+    q = m._bufs["q"]
+    o = m._bufs["o"]
+    ws = m._bufs["ws"]
+    reps = 20
+
+    def att():
+        ops.paged_attention(q, m.k_caches[0], m.v_caches[0], cu_q, cu_k, bt, 1, ctx0 + steps,
+                            m.scale, out=o, workspace=ws)
+
+    att()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s_):
+        att()
+    torch.cuda.current_stream().wait_stream(s_)
+    ga = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ga):
+        for li in range(reps):
+            ops.paged_attention(q, m.k_caches[li % len(m.k_caches)],
+                                m.v_caches[li % len(m.v_caches)], cu_q, cu_k, bt, 1,
+                                ctx0 + steps, m.scale, out=o, workspace=ws)
+    ga.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    ga.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    att_ms = _max_over_ranks(e0.elapsed_time(e1) / reps, world, dev)
+    ga.reset()
+    ctx_now = int(lens.sum().item())  # contexts of the last step (keys read per layer)
+    nbytes = ctx_now * m.hkv * 128 * 2 * 2 + 2 * B * m.hq * 128 * 2 + 4 * B * per
+    peak, peak_kind = load_peak()
+    gbs = nbytes / (att_ms * 1e-3) / 1e9
+    res = {"workload": "config 5: Qwen3-32B tp8, 64 sequences x 32768-token cached contexts "
+                       "(random KV), 128 greedy decode tokens each, CUDA graph per step",
+           "decode_tok_s": round(B * steps / (ms * 1e-3), 1),
+           "ms_per_step": round(ms / steps, 4),
+           "decode_attention": {"us_per_layer": round(att_ms * 1e3, 2), "bytes": int(nbytes),
+                                "achieved_gbs": round(gbs, 1), "peak": peak,
+                                "frac": round(gbs / peak, 4), "peak_source": peak_kind}}
+    m.close()
+    m.k_caches, m.v_caches = [], []
+    del m
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_nvkv(a):
     import torch
 
@@ -285,7 +635,7 @@ def run_nvkv(a):
         cfg = replace(cfg, num_hidden_layers=a.layers)
     w = workload()
     model = Qwen3TP(cfg, rank, world, seed=0, device=dev,
-                    peer_allreduce=not a.nccl_allreduce, max_tokens=NUM_SEQS)
+                    peer_allreduce=not a.nccl_allreduce, max_tokens=MAX_BATCHED)
     model.allocate_kv_cache(w["num_blocks"], PAGE, fill_random=True)
     host = {k: torch.from_numpy(np.ascontiguousarray(w[k])).pin_memory()
             for k in ("input_ids", "positions", "slot_mapping", "cu_q", "cu_k", "block_tables")}
@@ -409,6 +759,18 @@ def run_nvkv(a):
                            "busbw_gbs": round(pb, 1), "frac": round(pb / 900.0, 4),
                            "share_of_step": round(per_step * pm / (ms / a.steps), 4)}
 
+    parity = tp_parity(model.cfg, model.comm, world, rank, dev) if world > 1 else None
+    wl = None
+    if not a.no_workloads:  # whole workloads through the engine loop (every rank)
+        wl = {"config4": workload_config4(model, world, dev)}
+        if world == 1:
+            wl["config3_tp1"] = workload_config3(world, rank, dev, None)
+            wl["config1"] = workload_config1(dev)
+        elif world == 2:
+            wl["config3_tp2"] = workload_config3(world, rank, dev, model.comm)
+        elif world == 8:
+            wl["config5_tp8"] = workload_config5(world, rank, dev, model.comm)
+
     if rank == 0:
         peak, peak_kind = load_peak()
         nbytes = decode_bytes(w, model.hq, model.hkv)
@@ -435,6 +797,10 @@ def run_nvkv(a):
         }
         if ar is not None:
             line["collectives"] = ar
+        if parity is not None:
+            line["tp_parity"] = parity
+        if wl is not None:
+            line["workloads"] = wl
         if world == 1:
             line["cpu_baseline"] = cpu_reference()
             line["op_level"] = op_level_config2()

@@ -140,11 +140,13 @@ class Qwen3TP:
     def __init__(self, cfg: Qwen3Config, rank: int = 0, tp: int = 1, seed: int = 0,
                  dtype=torch.bfloat16, device="cuda", init_scale: float = 1.0, group=None,
                  embed_std: float = 1.0, head_std: Optional[float] = None,
-                 peer_allreduce: bool = True, max_tokens: int = 4096):
+                 peer_allreduce: bool = True, max_tokens: int = 4096, comm=None):
         """peer_allreduce (tp > 1): every all-reduce + the RMSNorm after it is one
         nvkv kernel over NVLink peer memory (nvkv.comm.PeerComm) instead of an
         NCCL call followed by nvkv_rms_norm; max_tokens bounds the tokens of a
-        step on that route."""
+        step on that route.  `comm` hands in an existing PeerComm of the same
+        ranks (kept open by its owner) instead of creating one.  With tp == 1
+        the model makes no collective call, even inside a multi-rank job."""
         self.cfg, self.rank, self.tp, self.group = cfg, rank, tp, group
         self.dtype, self.device = dtype, torch.device(device)
         self.hq = divide(cfg.num_attention_heads, tp)
@@ -194,16 +196,20 @@ class Qwen3TP:
         self.v_caches: List[torch.Tensor] = []
         self._bufs = {}
         self.comm = None
-        if tp > 1 and peer_allreduce:
+        self._own_comm = False
+        if tp > 1 and comm is not None:
+            self.comm = comm
+        elif tp > 1 and peer_allreduce:
+            self._own_comm = True
             from .comm import PeerComm
             self.comm = PeerComm(rank, tp, max_tokens * H * torch.tensor([], dtype=dtype)
                                  .element_size(), group=group)
 
     def close(self) -> None:
         """Releases the peer communicator (after every rank's last step)."""
-        if self.comm is not None:
+        if self.comm is not None and self._own_comm:
             self.comm.close()
-            self.comm = None
+        self.comm = None
 
     # ---- KV pool (model_runner.rs:286-303): per layer [Nb, P, Hkv/tp, D] ----
     def allocate_kv_cache(self, num_blocks: int, block_size: int = 256, fill_random: bool = False,
@@ -238,13 +244,17 @@ class Qwen3TP:
         """Qwen3ForCausalLM::forward + compute_logits (qwen3.rs:285-297,
         embed_head.rs:89-119): returns the full-vocab logits of each
         sequence's last token, [B, V], in the model dtype."""
-        return gather_logits(self._local_logits(st), self.group)
+        local = self._local_logits(st)
+        return gather_logits(local, self.group) if self.tp > 1 else local
 
     @torch.no_grad()
     def greedy(self, st: Step) -> torch.Tensor:
         """The greedy next token of every sequence, [B] int64: argmax of
         forward()'s logits, taken vocab-parallel (vocab_parallel_argmax)."""
-        return vocab_parallel_argmax(self._local_logits(st), self.rank, self.group)
+        local = self._local_logits(st)
+        if self.tp == 1:
+            return local.argmax(dim=-1)
+        return vocab_parallel_argmax(local, self.rank, self.group)
 
     def _local_logits(self, st: Step) -> torch.Tensor:
         """This rank's vocab shard of the last-token logits, [B, V/tp], model dtype."""
@@ -253,7 +263,10 @@ class Qwen3TP:
         cfg = self.cfg
         T = st.input_ids.numel()
         D = cfg.head_dim
-        h = vocab_parallel_embed(st.input_ids, self.embed, self.rank, self.group)
+        if self.tp > 1:
+            h = vocab_parallel_embed(st.input_ids, self.embed, self.rank, self.group)
+        else:
+            h = torch.nn.functional.embedding(st.input_ids, self.embed)
         q_buf = self._buf("q", (T, self.hq, D))
         o_buf = self._buf("o", (T, self.hq, D))
         ws_n = ops.workspace_size(st.cu_seqlens_q.numel() - 1, self.hq, self.hkv, st.max_seqlen_q,
