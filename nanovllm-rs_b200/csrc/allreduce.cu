@@ -35,8 +35,21 @@
 // input is rewritten by its next GEMM, after this kernel, and is only read
 // locally.
 //
+// Small messages (at most kArLLMaxBytes, e.g. a decode step's 256 x 4096
+// rows) take the low-latency (LL) form of the same two protocols instead:
+// every 8-byte word pushed to a peer carries 4 bytes of data and the call's
+// epoch in its upper half, stored and polled as single-copy-atomic 64-bit
+// words (st/ld.relaxed.sys).  The receiver spins on the words themselves, so
+// there is no CTA barrier and no system-scope release between the pushes and
+// the hand-off: a hand-off costs the data's flight time, at twice the bytes.
+// Large messages keep the flag hand-off, whose fixed cost is small next to
+// their transfer.  Both forms sum in the same order and give the same bits.
+//   LL buffers: recv_ll [2 parities][world][ll_region], gath_ll [2][ll_region]
+//   (ll_region = 2 x the data bytes of kArLLMaxBytes).
+//
 // Every wait is bounded by the communicator's timeout (%globaltimer); on
 // expiry the CTA records NVKV_DEVERR_PEER_TIMEOUT and returns.
+#include <algorithm>
 #include <cstring>
 #include <new>
 
@@ -46,11 +59,14 @@ namespace nvkv {
 
 constexpr int kArCtas = 148;
 constexpr int kArMaxRanks = NVKV_COMM_MAX_RANKS;
+constexpr size_t kArLLMaxBytes = (size_t)4 << 20;  // messages up to 4 MiB take the LL form
 
 struct ArParams {
   uint8_t* base[kArMaxRanks];  // every rank's allocation (same layout)
   int64_t region;              // bytes of one [max_tokens, hidden] buffer slot
   int64_t off_recv, off_gath, off_flag;
+  int64_t ll_region;           // bytes of one LL [rows, hidden] slot (2 x the data)
+  int64_t off_recv_ll, off_gath_ll;
   uint32_t* epoch;             // this rank's per-CTA epochs
   int rank, world;
   int two_shot;
@@ -104,6 +120,59 @@ __device__ __forceinline__ uint8_t* ar_recv(const ArParams& p, int q, int par, i
 }
 __device__ __forceinline__ uint8_t* ar_gath(const ArParams& p, int q, int par, int64_t row) {
   return p.base[q] + p.off_gath + (int64_t)par * p.region + row * p.H * 2;
+}
+
+// LL rows: 8-element vector c of a row (16 data bytes) is 4 words of 8 bytes,
+// data in the low half, the epoch in the high half.
+__device__ __forceinline__ uint8_t* ar_recv_ll(const ArParams& p, int q, int par, int src,
+                                               int64_t row) {
+  return p.base[q] + p.off_recv_ll + ((int64_t)par * p.world + src) * p.ll_region +
+         row * p.H * 4;
+}
+__device__ __forceinline__ uint8_t* ar_gath_ll(const ArParams& p, int q, int par, int64_t row) {
+  return p.base[q] + p.off_gath_ll + (int64_t)par * p.ll_region + row * p.H * 4;
+}
+// Pushes vector v (16 data bytes) as 4 LL words of epoch e at dst (32 bytes).
+__device__ __forceinline__ void st_ll(uint8_t* dst, uint4 v, uint32_t e) {
+  const uint64_t hi = (uint64_t)e << 32;
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(dst), "l"(hi | v.x),
+               "l"(hi | v.y)
+               : "memory");
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(dst + 16), "l"(hi | v.z),
+               "l"(hi | v.w)
+               : "memory");
+}
+// Polls the 4 LL words at src until all carry epoch e and returns their data;
+// gives up (zeros, *fail set, error recorded once) after timeout_ns or as
+// soon as another thread of the CTA has given up.
+__device__ __forceinline__ uint4 ld_ll(const uint8_t* src, uint32_t e, int64_t timeout_ns,
+                                       volatile int* fail, int* err) {
+  uint64_t a, b, c, d;
+  uint64_t t0 = 0;
+  for (uint32_t n = 0;; ++n) {
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];"
+                 : "=l"(a), "=l"(b)
+                 : "l"(src)
+                 : "memory");
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];"
+                 : "=l"(c), "=l"(d)
+                 : "l"(src + 16)
+                 : "memory");
+    if ((uint32_t)(a >> 32) == e && (uint32_t)(b >> 32) == e && (uint32_t)(c >> 32) == e &&
+        (uint32_t)(d >> 32) == e)
+      return make_uint4((uint32_t)a, (uint32_t)b, (uint32_t)c, (uint32_t)d);
+    if ((n & 63) == 0) {
+      if (n == 0) {
+        t0 = global_ns();
+      } else if (*fail || (int64_t)(global_ns() - t0) > timeout_ns) {
+        if (!*fail) {
+          *fail = 1;
+          record_error(err, NVKV_DEVERR_PEER_TIMEOUT);
+        }
+        return make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
 }
 
 // dtype(sum over ranks, rank order) of 8-element vector c of a row whose
@@ -242,6 +311,118 @@ __global__ void __launch_bounds__(kNormThreads) allreduce_rms_norm_kernel(const 
   if (tid == 0) p.epoch[b] = e;
 }
 
+// f32 sum in rank order of 8-element vectors, rounded once (as sum_vec).
+template <typename T>
+__device__ __forceinline__ uint4 sum_vals(const uint4* v, int W) {
+  float acc[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll
+  for (int q = 0; q < kArMaxRanks; ++q) {
+    if (q < W) {
+      const uint32_t* vp = reinterpret_cast<const uint32_t*>(&v[q]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = DT<T>::to_f2(vp[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    }
+  }
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) op[k] = DT<T>::from_f2(acc[2 * k], acc[2 * k + 1]);
+  return o;
+}
+
+// The LL form of the kernel above (same rows per CTA, same sums, same norm).
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) allreduce_rms_norm_ll_kernel(const ArParams p) {
+  __shared__ float red[kNormThreads / 32];
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_fail;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int W = p.world, r = p.rank, H = p.H, nvec = H / 8;
+  const int64_t rb = (int64_t)H * 2;  // data bytes per row
+  if (tid == 0) {
+    s_epoch = p.epoch[b] + 1;
+    s_fail = 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int par = (int)(e & 1u);
+  volatile int* fail = &s_fail;
+  const uint8_t* in = p.base[r];
+  T* res = reinterpret_cast<T*>(p.residual);
+  const T* wt = reinterpret_cast<const T*>(p.w);
+  T* out = reinterpret_cast<T*>(p.out);
+  auto mine = [&](int64_t u, int c) {
+    return __ldcg(reinterpret_cast<const uint4*>(in + u * rb + (int64_t)c * 16));
+  };
+
+  if (!p.two_shot) {
+    // ---- one-shot: push every row of this CTA to every peer, sum on arrival ----
+    for (int64_t u = b; u < p.T; u += kArCtas)
+      for (int c = tid; c < nvec; c += kNormThreads) {
+        const uint4 v = mine(u, c);
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < W && q != r) st_ll(ar_recv_ll(p, q, par, r, u) + (int64_t)c * 32, v, e);
+      }
+    for (int64_t u = b; u < p.T; u += kArCtas) {
+      T* ru = res + u * H;
+      norm_row_load<T>(
+          [&](int c) {
+            uint4 v[kArMaxRanks];
+#pragma unroll
+            for (int q = 0; q < kArMaxRanks; ++q)
+              if (q < W)
+                v[q] = q == r ? mine(u, c)
+                              : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
+                                      p.timeout_ns, fail, p.err);
+            return sum_vals<T>(v, W);
+          },
+          p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
+    }
+  } else {
+    // ---- two-shot: push each row to its owner; owners sum and push to all ----
+    for (int64_t u = b; u < p.T; u += kArCtas) {
+      const int o = (int)(u / p.S);
+      if (o == r) continue;
+      for (int c = tid; c < nvec; c += kNormThreads)
+        st_ll(ar_recv_ll(p, o, par, r, u) + (int64_t)c * 32, mine(u, c), e);
+    }
+    for (int64_t u = b; u < p.T; u += kArCtas) {
+      if ((int)(u / p.S) != r) continue;
+      for (int c = tid; c < nvec; c += kNormThreads) {
+        uint4 v[kArMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < W)
+            v[q] = q == r ? mine(u, c)
+                          : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
+                                  p.timeout_ns, fail, p.err);
+        const uint4 s = sum_vals<T>(v, W);
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < W) st_ll(ar_gath_ll(p, q, par, u) + (int64_t)c * 32, s, e);
+      }
+    }
+    for (int64_t u = b; u < p.T; u += kArCtas) {
+      T* ru = res + u * H;
+      norm_row_load<T>(
+          [&](int c) {
+            return ld_ll(ar_gath_ll(p, r, par, u) + (int64_t)c * 32, e, p.timeout_ns, fail,
+                         p.err);
+          },
+          p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && !s_fail) p.epoch[b] = e;
+}
+
 }  // namespace nvkv
 
 // ---------------------------------------------------------------------------
@@ -268,7 +449,13 @@ size_t recv_off(const nvkv_comm* c) { return c->region; }
 size_t gath_off(const nvkv_comm* c) { return c->region + 2 * (size_t)c->world * c->region; }
 size_t flag_off(const nvkv_comm* c) { return gath_off(c) + 2 * c->region; }
 size_t epoch_off(const nvkv_comm* c) { return flag_off(c) + round256(kFlagBytes); }
-size_t total_bytes(const nvkv_comm* c) { return epoch_off(c) + round256(kEpochBytes); }
+// LL slots hold 2 bytes of word per data byte, for messages up to kArLLMaxBytes
+size_t ll_region(const nvkv_comm* c) { return 2 * std::min(c->region, kArLLMaxBytes); }
+size_t recv_ll_off(const nvkv_comm* c) { return epoch_off(c) + round256(kEpochBytes); }
+size_t gath_ll_off(const nvkv_comm* c) {
+  return recv_ll_off(c) + 2 * (size_t)c->world * ll_region(c);
+}
+size_t total_bytes(const nvkv_comm* c) { return gath_ll_off(c) + 2 * ll_region(c); }
 
 // One-shot (every rank pushes its whole partial to every peer, one barrier)
 // for two ranks; two-shot (push to the row's owner, owner reduces and
@@ -412,6 +599,9 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   p.off_recv = (int64_t)recv_off(c);
   p.off_gath = (int64_t)gath_off(c);
   p.off_flag = (int64_t)flag_off(c);
+  p.ll_region = (int64_t)ll_region(c);
+  p.off_recv_ll = (int64_t)recv_ll_off(c);
+  p.off_gath_ll = (int64_t)gath_ll_off(c);
   p.epoch = reinterpret_cast<uint32_t*>(c->base + epoch_off(c));
   p.rank = c->rank;
   p.world = c->world;
@@ -428,9 +618,18 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   p.timeout_ns = c->timeout_ns;
   p.err = device_error_word();
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == NVKV_DTYPE_BF16)
-    allreduce_rms_norm_kernel<__nv_bfloat16><<<kArCtas, kNormThreads, 0, s>>>(p);
-  else
-    allreduce_rms_norm_kernel<__half><<<kArCtas, kNormThreads, 0, s>>>(p);
+  // every rank sees the same num_tokens, so every rank takes the same form
+  const bool ll = (size_t)num_tokens * (size_t)hidden * 2 <= kArLLMaxBytes;
+  if (dtype == NVKV_DTYPE_BF16) {
+    if (ll)
+      allreduce_rms_norm_ll_kernel<__nv_bfloat16><<<kArCtas, kNormThreads, 0, s>>>(p);
+    else
+      allreduce_rms_norm_kernel<__nv_bfloat16><<<kArCtas, kNormThreads, 0, s>>>(p);
+  } else {
+    if (ll)
+      allreduce_rms_norm_ll_kernel<__half><<<kArCtas, kNormThreads, 0, s>>>(p);
+    else
+      allreduce_rms_norm_kernel<__half><<<kArCtas, kNormThreads, 0, s>>>(p);
+  }
   return check_cuda(cudaGetLastError(), "allreduce_rms_norm launch");
 }

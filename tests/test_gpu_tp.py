@@ -12,7 +12,14 @@ steps fed with the TP=1 tokens, and requires:
     all-reduce + nvkv_rms_norm at TP2 (within one bf16 ulp of the sum at
     TP4).
 Both all-reduce routes of the model are run: the nvkv peer-memory kernel and
-NCCL.  Skipped with fewer GPUs than ranks.  NVLS is off (NCCL_NVLS_ENABLE=0).
+NCCL.
+
+The greedy-stream gate of tests/test_gpu_greedy.py also runs at TP2: the
+config-1 gate model sharded over two GPUs, free running and teacher forced,
+against the CPU restatement of the reference (bf16 rounding points) built
+from the same weights; >= 95 % of positions must agree.
+
+Skipped with fewer GPUs than ranks.  NVLS is off (NCCL_NVLS_ENABLE=0).
 """
 import os
 import socket
@@ -49,21 +56,57 @@ def _worker(rank, world, port, route, q):
         import nvkv
         from nvkv.comm import PeerComm
         from qwen3_config import QWEN3_8B
-        T = 256
-        comm = PeerComm(rank, world, T * QWEN3_8B.hidden_size * 2) if route == "peer" else None
-        res = bench.tp_parity(QWEN3_8B, comm, world, rank, dev, T=T, layers=2)
-        torch.cuda.synchronize()
-        assert nvkv.device_error() == 0
-        dist.barrier()
-        if comm is not None:
-            comm.close()
-        q.put((rank, "ok" if res["ok"] else repr(res)))
+        if route == "greedy":
+            msg = _greedy_tp(rank, world, dev)
+        else:
+            T = 256
+            comm = PeerComm(rank, world, T * QWEN3_8B.hidden_size * 2) if route == "peer" else None
+            res = bench.tp_parity(QWEN3_8B, comm, world, rank, dev, T=T, layers=2)
+            torch.cuda.synchronize()
+            assert nvkv.device_error() == 0
+            dist.barrier()
+            if comm is not None:
+                comm.close()
+            msg = "ok" if res["ok"] else repr(res)
+        q.put((rank, msg))
     except Exception as ex:  # pragma: no cover - reported to the parent
         q.put((rank, repr(ex)))
     finally:
         import torch.distributed as dist
         if dist.is_initialized():
             dist.destroy_process_group()
+
+
+def _greedy_tp(rank, world, dev):
+    """Config-1 gate model at TP=world vs the CPU reference stream."""
+    import torch.distributed as dist
+
+    import nvkv
+    import test_gpu_greedy as G
+    from nvkv.decoder import Qwen3TP
+    full = Qwen3TP(G.CFG, 0, 1, seed=3, device=dev, **G.GATE_INIT)  # every rank: TP1 weights
+    w = G.to_numpy_weights(full)
+    del full
+    model = Qwen3TP(G.CFG, rank, world, seed=3, device=dev, **G.GATE_INIT)
+    ref, tf, fr = [], [], []
+    for seed in (11, 12):
+        r = G.reference_stream(w, seed)
+        model.allocate_kv_cache(G.NB, G.P)
+        seqs, free = G.make_seqs(seed)
+        t = G.gpu_generate(model, seqs, 32, free, forced=r)
+        model.allocate_kv_cache(G.NB, G.P)
+        seqs, free = G.make_seqs(seed)
+        f = G.gpu_generate(model, seqs, 32, free)
+        ref += r
+        tf += t
+        fr += f
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == 0
+    dist.barrier()
+    model.close()
+    report = dict(free_running=G.agree(fr, ref), teacher_forced=G.agree(tf, ref))
+    ok = report["free_running"] >= 0.95 and report["teacher_forced"] >= 0.95
+    return "ok" if ok else repr(report)
 
 
 def _run(world, route):
@@ -89,3 +132,8 @@ def test_tp2_matches_tp1(route):
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
 def test_tp4_matches_tp1():
     _run(4, "peer")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_greedy_streams_match_cpu_reference():
+    _run(2, "greedy")
