@@ -46,19 +46,17 @@
 namespace nvkv {
 
 constexpr int kPfD = 128;
-constexpr int kPfBM = 128;                  // query rows per item
-constexpr int kPfBN = 64;                   // keys per S tile
-constexpr int kPfSlots = 10;                // K/V ring: K_j and V_j each take one slot
+constexpr int kPfBM = 128;
+constexpr int kPfBN = 128;
+constexpr int kPfSlots = 5;                 // K/V ring: K_j and V_j each take one slot
 constexpr int kPfThreads = 10 * 32;
-constexpr int kPfHalf = kPfBM * 128;        // Q: 128 rows x 128 B (64 elements)
-constexpr int kPfTile = 2 * kPfHalf;        // Q: 32 KB, 128 rows x 128 elements
-constexpr int kPfKvHalf = kPfBN * 128;      // K/V: 64 rows x 128 B
-constexpr int kPfKvTile = 2 * kPfKvHalf;    // K/V: 16 KB, 64 rows x 128 elements
+constexpr int kPfHalf = 128 * 128;          // 128 rows x 128 B (64 elements)
+constexpr int kPfTile = 2 * kPfHalf;        // 32 KB: 128 rows x 128 elements
 constexpr int kPfOffQA = 0;
 constexpr int kPfOffQB = kPfOffQA + kPfTile;
 constexpr int kPfOffKV = kPfOffQB + kPfTile;
-constexpr int kPfOffBar = kPfOffKV + kPfSlots * kPfKvTile;
-constexpr int kPfNumBars = 2 + 2 * kPfSlots + 10;
+constexpr int kPfOffBar = kPfOffKV + kPfSlots * kPfTile;
+constexpr int kPfNumBars = 2 + 2 * kPfSlots + 6;
 constexpr int kPfSmemBytes = kPfOffBar + kPfNumBars * 8 + 16 + 1024;
 constexpr uint32_t kPfTmemCols = 512;
 constexpr int kPfCtas = 148;  // B200 SMs
@@ -283,11 +281,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: kind::f16, fp32 accumulate, M = 128, N = n.
-__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, uint32_t b_mn_major,
-                                                  uint32_t n) {
-  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) |
-         ((uint32_t)(kPfBM >> 4) << 24);
+// Instruction descriptor: kind::f16, fp32 accumulate, M = N = 128.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, uint32_t b_mn_major) {
+  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) |
+         ((uint32_t)(kPfBN >> 3) << 17) | ((uint32_t)(kPfBM >> 4) << 24);
 }
 
 // Two P values -> one packed 16-bit pair (cvt.rn.*x2.f32, round to nearest
@@ -329,28 +326,25 @@ __device__ __forceinline__ float pf_exp_half(const float* sv, int kbase, int lim
   return rs.x + rs.y;
 }
 
-// S_x = Q_x . K^T over D = 128 (128 query rows x 64 keys): 8 MMAs of K = 16,
-// advancing 32 bytes inside the 128-byte swizzle atom (both operands K-major,
-// SWIZZLE_128B; the two 64-wide D halves of Q are kPfHalf apart, of K
-// kPfKvHalf apart).
+// S_x = Q_x . K^T over D = 128: 8 MMAs of K = 16, advancing 32 bytes inside
+// the 128-byte swizzle atom (both operands K-major, SWIZZLE_128B).
 __device__ __forceinline__ void pf_issue_s(uint32_t d_tmem, uint32_t sq, uint32_t sk,
                                            uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < kPfD / 16; ++kk) {
-    const uint32_t oq = (kk >> 2) * kPfHalf + (kk & 3) * 32;
-    const uint32_t ok = (kk >> 2) * kPfKvHalf + (kk & 3) * 32;
-    tc_mma(d_tmem, sdesc(sq + oq, 16, 1024), sdesc(sk + ok, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+    const uint32_t o = (kk >> 2) * kPfHalf + (kk & 3) * 32;
+    tc_mma(d_tmem, sdesc(sq + o, 16, 1024), sdesc(sk + o, 16, 1024), idesc, kk > 0 ? 1u : 0u);
   }
 }
-// O_x (+)= P_x . V over 64 keys: P_x in TMEM (lane = query row, 32 columns of
-// 16-bit key pairs over the S buffer's columns), 16 keys = 8 columns per MMA;
-// V MN-major in shared memory (D contiguous, the two 64-wide D halves
-// kPfKvHalf apart = LBO, 8 keys = SBO).
+// O_x (+)= P_x . V over 128 keys: P_x in TMEM (lane = query row, 64 columns of
+// 16-bit key pairs over the S_x columns), 16 keys = 8 columns per MMA; V
+// MN-major in shared memory (D contiguous, the two 64-wide D halves kPfHalf
+// apart = LBO, 8 keys = SBO).
 __device__ __forceinline__ void pf_issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv,
                                             uint32_t idesc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < kPfBN / 16; ++kk) {
-    const uint64_t bd = sdesc(sv + kk * 16 * 128, kPfKvHalf, 1024);
+    const uint64_t bd = sdesc(sv + kk * 16 * 128, kPfHalf, 1024);
     tc_mma_tmem_a(d_tmem, p_tmem + kk * 8, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
@@ -570,9 +564,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* q_empty = bars + 1;             // the item's last S MMA has read Q
   uint64_t* kv_full = bars + 2;             // [kPfSlots]
   uint64_t* kv_empty = kv_full + kPfSlots;  // [kPfSlots]
-  uint64_t* s_full = kv_empty + kPfSlots;   // [slot][buffer]: S written by the MMA
-  uint64_t* p_full = s_full + 4;            // [slot][buffer]: S read, P written
-  uint64_t* o_done = p_full + 4;            // [slot]: PV_x finished (O_x stable)
+  uint64_t* s_full = kv_empty + kPfSlots;   // [2]: S_x written by the MMA
+  uint64_t* p_full = s_full + 2;            // [2]: S_x read, P_x written (O_x rescaled / read)
+  uint64_t* o_done = p_full + 2;            // [2]: PV_x finished (O_x stable, P_x free)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -585,11 +579,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int x = 0; x < 4; ++x) {
+    for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 128);
+      mbar_init(&o_done[x], 1);
     }
-    for (int x = 0; x < 2; ++x) mbar_init(&o_done[x], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -602,44 +596,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // the work plan (and the inputs) of the kernels before this one
 
-  // TMEM columns: S_A buffers 0 / 1 at 0 / 64, S_B buffers at 128 / 192,
-  // O_A at 256, O_B at 384.  Key tile g of a slot (a running count over the
-  // CTA's items) uses S buffer g & 1; its phase on that buffer's barriers is
-  // (g >> 1) & 1.
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
-    // Ring order per item (the MMA warp's consumption order): K_0, K_1, then
-    // for every tile j: V_j, K_{j+2}.
     if (lane == 0) {
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
       uint32_t nq = 0, t = 0;  // items loaded, K/V ring loads (running over items)
       bool ok = true;
-      auto load_kv = [&](const PfItem& it, int j, bool v) -> bool {
-        const int s = (int)(t % kPfSlots);
-        const uint32_t ph = (t / kPfSlots) & 1u;
-        if (t >= kPfSlots && !mbar_wait(&kv_empty[s], ph ^ 1u, p.err)) return false;
-        const int j0 = j * kPfBN;
-        int64_t row;
-        if (p.block_tables) {
-          uint32_t page = p.block_tables[(int64_t)it.b * p.bt_stride + j0 / p.page_size];
-          if ((int64_t)page >= p.num_blocks) {
-            record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
-            page = 0;
-          }
-          row = (int64_t)page * p.page_size + (j0 % p.page_size);
-        } else {
-          row = (int64_t)it.ks + j0;
-        }
-        uint8_t* dst = smem + kPfOffKV + s * kPfKvTile;
-        const CUtensorMap* map = v ? &tmap_v : &tmap_k;
-        mbar_arrive_expect_tx(&kv_full[s], kPfKvTile);
-        tma_load_3d(dst, map, &kv_full[s], 0, it.kvh, (int)row);
-        tma_load_3d(dst + kPfKvHalf, map, &kv_full[s], 64, it.kvh, (int)row);
-        ++t;
-        return true;
-      };
       for (int k = 0; ok && (int64_t)k * gridDim.x < pf_num_items<kPlan>(p); ++k) {
         const int w = pf_work(k);
         PfItem it;
@@ -652,82 +616,104 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tma_load_3d(qd + kPfHalf, &tmap_q, q_full, 64, it.head0 + x, (int)(it.qs + it.i0));
         }
         ++nq;
-        const int n = it.ntiles;
-        ok = load_kv(it, 0, false) && (n < 2 || load_kv(it, 1, false));
-        for (int j = 0; ok && j < n; ++j)
-          ok = load_kv(it, j, true) && (j + 2 >= n || load_kv(it, j + 2, false));
+        for (int u = 0; u < 2 * it.ntiles; ++u, ++t) {  // K_0, V_0, K_1, V_1, ...
+          const int j = u >> 1;
+          const int s = (int)(t % kPfSlots);
+          const uint32_t ph = (t / kPfSlots) & 1u;
+          if (t >= kPfSlots && !mbar_wait(&kv_empty[s], ph ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          const int j0 = j * kPfBN;
+          int64_t row;
+          if (p.block_tables) {
+            uint32_t page = p.block_tables[(int64_t)it.b * p.bt_stride + j0 / p.page_size];
+            if ((int64_t)page >= p.num_blocks) {
+              record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
+              page = 0;
+            }
+            row = (int64_t)page * p.page_size + (j0 % p.page_size);
+          } else {
+            row = (int64_t)it.ks + j0;
+          }
+          uint8_t* dst = smem + kPfOffKV + s * kPfTile;
+          const CUtensorMap* map = (u & 1) ? &tmap_v : &tmap_k;
+          mbar_arrive_expect_tx(&kv_full[s], kPfTile);
+          tma_load_3d(dst, map, &kv_full[s], 0, it.kvh, (int)row);
+          tma_load_3d(dst + kPfHalf, map, &kv_full[s], 64, it.kvh, (int)row);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
-    // Per item: S_A(0), S_B(0), S_A(1), S_B(1); then for every tile j:
-    // PV_A(j), S_A(j+2), PV_B(j), S_B(j+2).  S(j+2) reuses the buffer of
-    // P(j), so it is issued after PV(j) on the in-order tensor pipe, and it
-    // runs while the softmax warps work on tile j+1.
     if (lane == 0) {
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      constexpr uint32_t idesc_qk = make_idesc(fmt, 0u, kPfBN);
-      constexpr uint32_t idesc_pv = make_idesc(fmt, 1u, kPfD);
+      constexpr uint32_t idesc_qk = make_idesc(fmt, 0u);
+      constexpr uint32_t idesc_pv = make_idesc(fmt, 1u);
       const uint32_t kv0 = smem_u32(smem + kPfOffKV);
-      const uint32_t sq[2] = {smem_u32(smem + kPfOffQA), smem_u32(smem + kPfOffQB)};
+      const uint32_t sqa = smem_u32(smem + kPfOffQA), sqb = smem_u32(smem + kPfOffQB);
+#define PF_SLOT(t) (kv0 + (uint32_t)((t) % kPfSlots) * kPfTile)
+#define PF_PAR(t) ((uint32_t)((t) / kPfSlots) & 1u)
+#define PF_FULL(t) (&kv_full[(t) % kPfSlots])
       uint32_t nq = 0, t = 0, g = 0;  // items, K/V ring position, key tiles per slot
       bool ok = true;
-      // waits for ring entry t (loaded) and returns its shared-memory address
-      auto ring = [&](uint32_t tt, uint32_t* addr) -> bool {
-        if (!mbar_wait(&kv_full[tt % kPfSlots], (tt / kPfSlots) & 1u, p.err)) return false;
-        tc_fence_after();
-        *addr = kv0 + (tt % kPfSlots) * (uint32_t)kPfKvTile;
-        return true;
-      };
-      // S_x(gg) for both slots from K at ring entry tt, then frees the entry
-      auto issue_s = [&](uint32_t tt, uint32_t gg) -> bool {
-        uint32_t ka;
-        if (!ring(tt, &ka)) return false;
-        for (int x = 0; x < nslot; ++x) {
-          pf_issue_s(tmem + (uint32_t)x * 128u + (gg & 1u) * 64u, sq[x], ka, idesc_qk);
-          tc_commit(&s_full[x * 2 + (gg & 1u)]);
-        }
-        tc_commit(&kv_empty[tt % kPfSlots]);
-        return true;
-      };
       for (int k = 0; ok && (int64_t)k * gridDim.x < pf_num_items<kPlan>(p); ++k) {
         const int w = pf_work(k);
         PfItem it;
         if (w >= pf_num_items<kPlan>(p) || !pf_item<kPlan>(p, w, it)) continue;
         const int n = it.ntiles;
-        ok = mbar_wait(q_full, nq & 1u, p.err);
+        // S_x(g) of the item's first key tile: Q and K_0 (S_x / P_x(g - 1) were
+        // consumed by PV_x(g - 1), issued before it on the in-order pipe)
+        ok = mbar_wait(q_full, nq & 1u, p.err) && mbar_wait(PF_FULL(t), PF_PAR(t), p.err);
         if (!ok) break;
+        tc_fence_after();
+        pf_issue_s(tmem + 0u, sqa, PF_SLOT(t), idesc_qk);
+        tc_commit(&s_full[0]);
+        if (p.pair) {
+          pf_issue_s(tmem + 128u, sqb, PF_SLOT(t), idesc_qk);
+          tc_commit(&s_full[1]);
+        }
+        tc_commit(&kv_empty[t % kPfSlots]);
+        if (n == 1) tc_commit(q_empty);
         ++nq;
-        // S(0), S(1): their buffers last held P(g-2), P(g-1), consumed by PVs
-        // already issued (in-order pipe)
-        ok = issue_s(t++, g);
-        if (ok && n >= 2) ok = issue_s(t++, g + 1);
-        if (!ok) break;
-        if (n <= 2) tc_commit(q_empty);  // the item's last S MMAs read Q
         for (int j = 0; j < n; ++j, ++g) {
-          const uint32_t bb = g & 1u, ph = (g >> 1) & 1u;
-          uint32_t va;
-          ok = ring(t++, &va);
+          const uint32_t pj = g & 1u;
+          const bool more = j + 1 < n;
+          const uint32_t tv = t + 2 * j + 1, tk = t + 2 * j + 2;  // V_j, K_{j+1}
+          ok = mbar_wait(PF_FULL(tv), PF_PAR(tv), p.err) && mbar_wait(&p_full[0], pj, p.err);
           if (!ok) break;
-          const uint32_t tv = t - 1;
-          const bool more = j + 2 < n;
-          for (int x = 0; x < nslot; ++x) {
-            ok = mbar_wait(&p_full[x * 2 + bb], ph, p.err);
+          tc_fence_after();
+          pf_issue_pv(tmem + 256u, tmem + 0u, PF_SLOT(tv), idesc_pv, j > 0);
+          tc_commit(&o_done[0]);
+          if (more) {
+            ok = mbar_wait(PF_FULL(tk), PF_PAR(tk), p.err);
             if (!ok) break;
             tc_fence_after();
-            pf_issue_pv(tmem + 256u + (uint32_t)x * 128u, tmem + (uint32_t)x * 128u + bb * 64u, va,
-                        idesc_pv, j > 0);
-            tc_commit(&o_done[x]);
+            pf_issue_s(tmem + 0u, sqa, PF_SLOT(tk), idesc_qk);
+            tc_commit(&s_full[0]);
           }
-          if (!ok) break;
-          tc_commit(&kv_empty[tv % kPfSlots]);  // V_j: every P.V issued
-          if (more) {
-            ok = issue_s(t++, g + 2);
+          if (p.pair) {
+            ok = mbar_wait(&p_full[1], pj, p.err);
             if (!ok) break;
-            if (j + 3 == n) tc_commit(q_empty);
+            tc_fence_after();
+            pf_issue_pv(tmem + 384u, tmem + 128u, PF_SLOT(tv), idesc_pv, j > 0);
+            tc_commit(&o_done[1]);
+          }
+          tc_commit(&kv_empty[tv % kPfSlots]);  // V_j: both P.V issued
+          if (more) {
+            if (p.pair) {
+              pf_issue_s(tmem + 128u, sqb, PF_SLOT(tk), idesc_qk);
+              tc_commit(&s_full[1]);
+            }
+            tc_commit(&kv_empty[tk % kPfSlots]);  // K_{j+1}: both S issued
+            if (j + 2 == n) tc_commit(q_empty);   // the item's last S MMAs read Q
           }
         }
+        t += 2 * (uint32_t)n;
       }
+#undef PF_SLOT
+#undef PF_PAR
+#undef PF_FULL
     }
   } else {
     // ------------------------------ softmax warpgroups ------------------------------
@@ -736,7 +722,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int quarter = warp & 3;  // TMEM lane quarter this warp may access
       const int r = quarter * 32 + lane;
       const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-      const uint32_t col_o = 256u + (uint32_t)x * 128u;
+      const uint32_t col_s = x ? 128u : 0u, col_o = x ? 384u : 256u;
       uint32_t g = 0;  // key tiles of this slot so far (running over items)
       bool alive = true;
       for (int k = 0; alive && (int64_t)k * gridDim.x < pf_num_items<kPlan>(p); ++k) {
@@ -747,10 +733,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int lim_row = p.causal ? min(it.k_len - 1, qi + it.off) : it.k_len - 1;
         float m_ref = -INFINITY, l = 0.f;
         for (int j = 0; j < it.ntiles; ++j, ++g) {
-          const uint32_t bb = g & 1u, ph = (g >> 1) & 1u;
-          const uint32_t col_s = (uint32_t)x * 128u + bb * 64u;
-          // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned
-          if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x * 2 + bb], ph, p.err))) {
+          const uint32_t pj = g & 1u;
+          // decisions stay warp-uniform: the tcgen05.ld/st below are .sync.aligned.
+          // s_full(g) also means PV_x(g - 1) is complete (it was issued before
+          // S_x(g)): O_x is stable for a rescale.
+          if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], pj, p.err))) {
             alive = false;
             break;
           }
@@ -758,20 +745,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const int lim = lim_row - j * kPfBN;  // keys c <= lim are visible
           // the whole warp sees every key of this tile: no masking needed
           const bool vis = __all_sync(0xffffffffu, lim >= kPfBN - 1);
-          // the tile's S row in registers: one TMEM round trip, exact tile max
-          float sv[kPfBN];
+          // the whole S row in registers: one TMEM round trip, exact tile max
+          float sv[128];
           tmem_ld32(lane_addr + col_s, sv);
           tmem_ld32(lane_addr + col_s + 32, sv + 32);
+          tmem_ld32(lane_addr + col_s + 64, sv + 64);
+          tmem_ld32(lane_addr + col_s + 96, sv + 96);
           tmem_wait_ld();
           // four independent max chains, then combined
           float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
           if (vis) {
 #pragma unroll
-            for (int i = 0; i < kPfBN; i += 2)
-              m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], sv[i], sv[i + 1]);
+            for (int i = 0; i < 128; i += 2) m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], sv[i], sv[i + 1]);
           } else {
 #pragma unroll
-            for (int i = 0; i < kPfBN; i += 2)
+            for (int i = 0; i < 128; i += 2)
               m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], i <= lim ? sv[i] : -INFINITY,
                                        i + 1 <= lim ? sv[i + 1] : -INFINITY);
           }
@@ -784,8 +772,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const float fac = need ? exp2f(m_ref - m_new) : 1.f;
           if (j == 0 || need) m_ref = m_new;
           const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-          // P over the S columns just read: keys 0-63 -> the buffer's first 32
-          // columns (the PV MMA's A operand)
+          // P_x over the S_x columns just read: keys 0-63 -> columns 0-31,
+          // keys 64-127 -> columns 32-63 (the PV MMA's A operand)
           float rs;
           {
             uint32_t pk[32];
@@ -793,14 +781,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                      : pf_exp_half<T, true>(sv, 0, lim, p.scale_log2, m_use, pk);
             tmem_st32(lane_addr + col_s, reinterpret_cast<const float*>(pk));
           }
+          {
+            uint32_t pk[32];
+            rs += vis ? pf_exp_half<T, false>(sv + 64, 64, lim, p.scale_log2, m_use, pk)
+                      : pf_exp_half<T, true>(sv + 64, 64, lim, p.scale_log2, m_use, pk);
+            tmem_st32(lane_addr + col_s + 32, reinterpret_cast<const float*>(pk));
+          }
           if (rescale) {  // O_x *= 2^(m_old - m_new) before PV_x(g) adds to it
-            // PV_x(g - 1) may still be running (S(g) was issued after
-            // PV_x(g - 2) only): wait for it before touching O_x
-            if (!__all_sync(0xffffffffu, mbar_wait(&o_done[x], (g - 1u) & 1u, p.err))) {
-              alive = false;
-              break;
-            }
-            tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < 8; ++c) {
               float o[16];
@@ -815,7 +802,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tmem_wait_st();
           l += rs;
           tc_fence_before();
-          mbar_arrive(&p_full[x * 2 + bb]);
+          mbar_arrive(&p_full[x]);
         }
         // the item's last PV_x: O_x complete
         if (!alive ||

@@ -140,17 +140,13 @@ class Qwen3TP:
     def __init__(self, cfg: Qwen3Config, rank: int = 0, tp: int = 1, seed: int = 0,
                  dtype=torch.bfloat16, device="cuda", init_scale: float = 1.0, group=None,
                  embed_std: float = 1.0, head_std: Optional[float] = None,
-                 peer_allreduce: bool = True, max_tokens: int = 4096, comm=None,
-                 head_row_sigma: float = 0.0):
+                 peer_allreduce: bool = True, max_tokens: int = 4096, comm=None):
         """peer_allreduce (tp > 1): every all-reduce + the RMSNorm after it is one
         nvkv kernel over NVLink peer memory (nvkv.comm.PeerComm) instead of an
         NCCL call followed by nvkv_rms_norm; max_tokens bounds the tokens of a
         step on that route.  `comm` hands in an existing PeerComm of the same
         ranks (kept open by its owner) instead of creating one.  With tp == 1
-        the model makes no collective call, even inside a multi-rank job.
-        head_row_sigma > 0 scales each lm_head row by exp(sigma * z), z ~ N(0, 1)
-        (seeded): a random-init head whose top logits stand further apart, so
-        greedy streams of two implementations are not decided by near-ties."""
+        the model makes no collective call, even inside a multi-rank job."""
         self.cfg, self.rank, self.tp, self.group = cfg, rank, tp, group
         self.dtype, self.device = dtype, torch.device(device)
         self.hq = divide(cfg.num_attention_heads, tp)
@@ -194,11 +190,6 @@ class Qwen3TP:
         self.norm = norm_w(H)
         lm = emb if cfg.tie_word_embeddings else full(cfg.vocab_size, H,
                                                        s_in if head_std is None else head_std)
-        if head_row_sigma > 0:
-            self._n += 1
-            g = torch.Generator(device=self.device).manual_seed(seed * 1000003 + self._n)
-            z = torch.randn(cfg.vocab_size, 1, generator=g, device=self.device)
-            lm = (lm.float() * torch.exp(head_row_sigma * z)).to(dtype)
         self.lm_head = shard_vocab(lm, rank, tp)  # tie_weights (qwen3.rs:334-338)
         del emb, lm
         self.k_caches: List[torch.Tensor] = []
