@@ -621,6 +621,93 @@ def workload_config5(world, rank, dev, comm, steps=128):
     return res
 
 
+def kv_fp8_step(model, w, world, dev, steps, warmup):
+    """The same decode step over the optional fp8 (e4m3) pool: K/V codes with
+    a f32 scale per (slot, kv head) row, written by the fp8 store, read by the
+    fp8 decode kernel at half the bytes.  Not the reference's format (its pool
+    is in the model dtype), so it is reported beside the headline, never as
+    it.  CUDA graph of one step replayed `steps` times, CUDA events, worst
+    rank; plus the decode attention of all layers, graph-replayed, against the
+    measured HBM peak (algorithmic bytes: one byte per K/V value plus the
+    4-byte row scales, q, out, block tables)."""
+    import torch
+
+    from nvkv import ops
+    from nvkv.decoder import Step
+    model.k_caches, model.v_caches = [], []
+    torch.cuda.empty_cache()
+    model.allocate_kv_cache(w["num_blocks"], PAGE, fill_random=True, kv_fp8=True)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    st = Step(t(w["input_ids"]), t(w["positions"]), t(w["slot_mapping"]), t(w["cu_q"]),
+              t(w["cu_k"]), t(w["block_tables"]), torch.arange(NUM_SEQS, device=dev), 1, w["max_k"])
+    for _ in range(max(1, warmup)):
+        model.greedy(st)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        model.greedy(st)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        model.greedy(st)
+    g.replay()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    g.reset()
+    q, o, ws = model._bufs["q"], model._bufs["o"], model._bufs["ws"]
+    L = model.cfg.num_hidden_layers
+
+    def att():
+        for li in range(L):
+            ops.paged_attention_fp8(q, model.k_caches[li], model.v_caches[li], model.k_scales[li],
+                                    model.v_scales[li], st.cu_seqlens_q, st.cu_seqlens_k,
+                                    st.block_tables, 1, w["max_k"], model.scale, out=o,
+                                    workspace=ws)
+
+    att()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(side):
+        att()
+    torch.cuda.current_stream().wait_stream(side)
+    ga = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ga):
+        att()
+    ga.replay()
+    torch.cuda.synchronize()
+    reps = max(3, min(steps, 20))
+    e0.record()
+    for _ in range(reps):
+        ga.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    kern_ms = _max_over_ranks(e0.elapsed_time(e1) / (reps * L), world, dev)
+    ga.reset()
+    ctx = int(w["ctx"].sum())
+    nbytes = (ctx * model.hkv * (128 + 4) * 2 + 2 * NUM_SEQS * model.hq * 128 * 2 +
+              4 * int(((w["ctx"] + PAGE - 1) // PAGE).sum()) + 8 * (NUM_SEQS + 1))
+    peak, kind = load_peak()
+    gbs = nbytes / (kern_ms * 1e-3) / 1e9
+    res = {"value": round(NUM_SEQS * steps / (ms * 1e-3), 1), "unit": "tok/s",
+           "ms_per_step": round(ms / steps, 4),
+           "kv": "e4m3 codes + f32 scale per (slot, kv head) row; not the reference's format",
+           "decode_attention": {"us_per_launch": round(kern_ms * 1e3, 2), "bytes": int(nbytes),
+                                "achieved_gbs": round(gbs, 1), "peak": peak,
+                                "frac": round(gbs / peak, 4), "peak_source": kind}}
+    model.k_caches, model.v_caches, model.k_scales, model.v_scales = [], [], [], []
+    model.kv_fp8 = False
+    model._bufs.pop("ws", None)
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_nvkv(a):
     import torch
 
@@ -760,6 +847,7 @@ def run_nvkv(a):
                            "share_of_step": round(per_step * pm / (ms / a.steps), 4)}
 
     parity = tp_parity(model.cfg, model.comm, world, rank, dev) if world > 1 else None
+    kv8 = None if a.no_workloads else kv_fp8_step(model, w, world, dev, a.steps, a.warmup)
     wl = None
     if not a.no_workloads:  # whole workloads through the engine loop (every rank)
         wl = {"config4": workload_config4(model, world, dev)}
@@ -799,6 +887,8 @@ def run_nvkv(a):
             line["collectives"] = ar
         if parity is not None:
             line["tp_parity"] = parity
+        if kv8 is not None:
+            line["kv_fp8"] = kv8
         if wl is not None:
             line["workloads"] = wl
         if world == 1:

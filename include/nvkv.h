@@ -168,6 +168,55 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
                          nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * FP8 (e4m3) KV pool: an optional pool format at half the bytes.
+ * No counterpart in the reference, whose pool is in the model dtype
+ * (nanovllm_rs/src/engine/model_runner.rs:286-303); it stands beside the
+ * store of kv_cache.rs:168-190 and the attention of attention.rs:37-75.
+ *
+ * Layout: k_cache / v_cache [num_blocks, page_size, Hkv, 128] one-byte e4m3
+ * codes (the dtype pool's slot addressing); k_scale / v_scale
+ * [num_blocks, Hkv, page_size] f32, one scale per (slot, kv head) row:
+ *   scale = amax / 448, code = e4m3_rn_satfinite(x * (448 / amax)),
+ *   value = code * scale   (amax = max |x| over the row's 128 values; a row
+ *   of zeros gets scale 0).  Division and product are f32, rounded to nearest.
+ *
+ * nvkv_store_kvcache_fp8: quantises rows t < num_tokens of key/value
+ * ([T, Hkv, 128] bf16/f16 with token strides key_stride / value_stride
+ * elements, a multiple of 4; rows 8-byte aligned) into slot slot_mapping[t]
+ * (negative: skipped; >= num_blocks * page_size: skipped, recorded as
+ * NVKV_DEVERR_SLOT_RANGE).  Bit-exact with the formula above.
+ *
+ * nvkv_paged_attention_fp8: nvkv_paged_attention over an fp8 pool (paged
+ * only: block_tables required; page_size a multiple of 128).  q/out are
+ * bf16/f16 as `dtype`.  Decode rows read the codes directly (half the bytes);
+ * prompt rows (q_len > 1) are dequantised into the workspace first, so the
+ * caller passes prompt_kv_tokens >= the sum of k_len over the batch's
+ * q_len > 1 sequences (0 when max_seqlen_q <= 1); a prompt that does not fit
+ * is skipped and reported as NVKV_DEVERR_SEQLEN.  The workspace holds
+ * nvkv_paged_attention_fp8_workspace_size() bytes.  Outputs are the attention
+ * of q over the dequantised keys and values (values rounded to the dtype).
+ * ---------------------------------------------------------------------- */
+int nvkv_store_kvcache_fp8(const void* key, const void* value, void* k_cache, void* v_cache,
+                           float* k_scale, float* v_scale, const int64_t* slot_mapping,
+                           int64_t num_tokens, int num_kv_heads, int head_dim,
+                           int64_t key_stride, int64_t value_stride, int64_t num_blocks,
+                           int page_size, int dtype, nvkv_stream_t stream);
+
+int nvkv_paged_attention_fp8_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
+                                            int head_dim, int max_seqlen_q, int max_seqlen_k,
+                                            int64_t prompt_kv_tokens, size_t* bytes);
+
+int nvkv_paged_attention_fp8(const void* q, int64_t q_stride, int64_t num_q_tokens,
+                             const void* k_cache, const void* v_cache, const float* k_scale,
+                             const float* v_scale, int64_t num_blocks, void* out,
+                             const uint32_t* cu_seqlens_q, const uint32_t* cu_seqlens_k,
+                             const uint32_t* block_tables, int64_t block_table_stride,
+                             int num_seqs, int max_seqlen_q, int max_seqlen_k, int num_q_heads,
+                             int num_kv_heads, int head_dim, int page_size, float softmax_scale,
+                             int causal, int64_t prompt_kv_tokens, void* workspace,
+                             size_t workspace_bytes, int dtype, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * nvkv_paged_attention without a workspace argument, for callers that cannot
  * allocate device memory on the call path (an engine that has handed nearly
  * all free GPU memory to its KV pool, code inside a stream capture that may

@@ -146,6 +146,40 @@ def case_decode(name, lens, hq, hkv, nblocks, iters, copies=1):
                 splits=bool(ops.workspace_size(B, hq, hkv, 1, int(max(lens)))), bound="hbm")
 
 
+def case_decode_fp8(name, lens, hq, hkv, nblocks, iters, copies=1):
+    """case_decode over the fp8 (e4m3) pool: codes and per-row scales written
+    by nvkv_store_kvcache_fp8 from random rows.  Algorithmic bytes: one byte
+    per K/V value plus the 4-byte row scales, q and out, block tables."""
+    page = 256
+    caches, bt = _paged(lens, page, hkv, nblocks, 3, copies)
+    pools = []
+    slots = torch.arange(nblocks * page, device="cuda")
+    for kc, vc in caches:
+        k8 = torch.empty(nblocks, page, hkv, 128, dtype=torch.uint8, device="cuda")
+        v8 = torch.empty_like(k8)
+        ks = torch.empty(nblocks, hkv, page, dtype=torch.float32, device="cuda")
+        vs = torch.empty_like(ks)
+        ops.store_kvcache_fp8(kc.view(-1, hkv, 128), vc.view(-1, hkv, 128), k8, v8, ks, vs, slots)
+        pools.append((k8, v8, ks, vs))
+    del caches
+    torch.cuda.empty_cache()
+    B = len(lens)
+    q = torch.randn(B, hq, 128, device="cuda").bfloat16()
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    cu_k = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).cuda()
+    out = torch.empty_like(q)
+    ws = torch.empty(max(16, ops.workspace_size_fp8(B, hq, hkv, 1, int(max(lens)), 0)),
+                     dtype=torch.uint8, device="cuda")
+    fn = lambda i: ops.paged_attention_fp8(q, *pools[i % copies], cu_q, cu_k, bt, 1,  # noqa
+                                           int(max(lens)), 128 ** -0.5, out=out, workspace=ws)
+    med, _ = _time(fn, iters)
+    nblk = sum((int(L) + page - 1) // page for L in lens)
+    nbytes = (int(np.sum(lens)) * hkv * (128 + 4) * 2 + 2 * B * hq * 128 * 2 + 4 * nblk +
+              8 * (B + 1))
+    return dict(kernel=name, B=B, hq=hq, hkv=hkv, L_mean=float(np.mean(lens)), bytes=nbytes, s=med,
+                bound="hbm", kv="e4m3 + f32 row scales")
+
+
 def case_step_metadata(B, iters, P=256):
     """nvkv_decode_advance on a B-sequence decode step (lengths U[1025,1536],
     pages appended ahead): the device replacement of the host-side metadata
@@ -386,6 +420,14 @@ CASES = {
                                               [1536]]), 4, 1, 600, it, 8),
     "decode_32b_tp8": lambda it: case_decode(
         "decode_32b_tp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
+    "decode_8b_tp1_fp8": lambda it: case_decode_fp8(
+        "decode_8b_tp1_fp8", np.random.default_rng(4).integers(1025, 1537, 256), 32, 8, 1560, it,
+        2),
+    "decode_8b_tp8_fp8": lambda it: case_decode_fp8(
+        "decode_8b_tp8_fp8", np.random.default_rng(4).integers(1025, 1537, 256), 4, 1, 1560, it,
+        8),
+    "decode_32b_tp8_fp8": lambda it: case_decode_fp8(
+        "decode_32b_tp8_fp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
     "prefill_8b": lambda it: case_prefill(it),
     "step_metadata": lambda it: case_step_metadata(256, it),
     "mixed_4b_tp1": lambda it: case_mixed(it, 1),

@@ -11,7 +11,7 @@
 
 namespace nvkv {
 
-static int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, int d) {
+int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, int d) {
   if (num_seqs < 0 || max_q < 0 || max_k < 0)
     return set_error(NVKV_ERR_INVALID_ARG, "paged_attention: negative size");
   if (d != 128) return set_error(NVKV_ERR_UNSUPPORTED, "paged_attention: head_dim must be 128");
@@ -25,7 +25,7 @@ static int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, 
 }
 
 // Split-KV decode scratch, then (for max_seqlen_q > 1) the prefill work plan.
-static size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k) {
+size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k) {
   if (num_seqs <= 0) return 0;
   const size_t dec = decode_workspace_bytes(num_seqs, hq, hkv, max_k);
   const size_t plan = prefill_plan_bytes(num_seqs, max_q);

@@ -56,6 +56,12 @@ int encode_kv_tensor_map(CUtensorMap* map, const void* base, int64_t head_dim,
                          int64_t num_heads, int64_t num_rows, int64_t row_stride_bytes,
                          int box_inner, int box_rows, bool swizzle128);
 
+// The same for an fp8 (1-byte) pool: box = one head's row_bytes (128) x
+// box_rows rows, SWIZZLE_128B.
+int encode_kv_tensor_map_u8(CUtensorMap* map, const void* base, int64_t row_bytes,
+                            int64_t num_heads, int64_t num_rows, int64_t row_stride_bytes,
+                            int box_rows);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Raises a kernel's dynamic shared-memory limit once per device (first call
@@ -84,8 +90,16 @@ struct AttnArgs {
   size_t ws_bytes;
   int dtype;
   cudaStream_t stream;
+  // fp8 (e4m3) pool: per (page, kv head, row) f32 scales [num_blocks, Hkv,
+  // page]; null for a bf16/f16 pool
+  const float* k_scale = nullptr;
+  const float* v_scale = nullptr;
 };
 
+// Shared by the attention entry points (api.cu): shape checks, and the
+// workspace of split-KV scratch + prefill work plan.
+int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, int d);
+size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k);
 int launch_paged_decode(const AttnArgs& a);
 size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k);
 void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,

@@ -100,6 +100,27 @@ int encode_kv_tensor_map(CUtensorMap* map, const void* base, int64_t head_dim, i
   return NVKV_OK;
 }
 
+int encode_kv_tensor_map_u8(CUtensorMap* map, const void* base, int64_t row_bytes,
+                            int64_t num_heads, int64_t num_rows, int64_t row_stride_bytes,
+                            int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  int rc = get_encoder(&encode);
+  if (rc) return rc;
+  // dim0 = the head's bytes (contiguous), dim1 = heads, dim2 = rows (slots)
+  cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)num_heads, (cuuint64_t)num_rows};
+  cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)row_stride_bytes};
+  cuuint32_t box[3] = {(cuuint32_t)row_bytes, 1u, (cuuint32_t)box_rows};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NVKV_ERR_CUDA, "cuTensorMapEncodeTiled (u8) failed (code " +
+                                        std::to_string((int)r) + ")");
+  return NVKV_OK;
+}
+
 }  // namespace nvkv
 
 extern "C" {

@@ -47,26 +47,97 @@ struct DecodeParams {
   float* ws_o;    // [B][max_splits][Hq][D]
   float* ws_lse;  // [B][max_splits][Hq]
   int* err;
+  const float* k_scale;  // fp8 pool: [num_blocks][Hkv][page_size] f32
+  const float* v_scale;
+  int num_kv_heads;
 };
 
-template <typename T, bool kHi>
-__global__ void __launch_bounds__(kDecThreads, 2)
+// fp8 (e4m3) pool: the producer stages each tile's K and V codes (64 rows x
+// 128 B, one TMA box each) in a 2-stage fp8 ring; two converter warps turn
+// them into the dtype tiles (x * its row's scale, rounded once) of a
+// 2-stage ring in exactly the layout TMA gives the bf16 kernel, so the
+// compute warps run the same per-tile code.  HBM sees half the K/V bytes.
+constexpr int kDec8Stages = 2;
+constexpr int kDec8ConvWarps = 2;
+constexpr int kDec8Threads = (kDecComputeWarps + 1 + kDec8ConvWarps) * 32;
+constexpr int kDec8CodeTile = kDecTile * kDecD;        // 8 KB of codes: one K (or V) tile
+constexpr int kDec8CodeStage = 2 * kDec8CodeTile;       // K + V codes
+constexpr int kDec8OffCodes = kDec8Stages * kDecStageBytes;
+constexpr int kDec8OffRow = kDec8OffCodes + kDec8Stages * kDec8CodeStage;
+constexpr int kDec8OffBars = kDec8OffRow + kDec8Stages * 8;
+constexpr int kDec8SmemBytes =
+    kDec8OffBars + 4 * kDec8Stages * 8 + kDecComputeWarps * 2 * 16 * 4 + 1024;
+static_assert(2 * kDec8SmemBytes <= 228 * 1024, "fp8 decode: two CTAs per SM");
+
+// Four e4m3 codes (a 32-bit word, lowest byte first) -> four floats.
+__device__ __forceinline__ void e4m3x4_to_f32(uint32_t w, float* f) {
+  uint32_t lo, hi;
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+  const float2 a = __half22float2(*reinterpret_cast<__half2*>(&lo));
+  const float2 b = __half22float2(*reinterpret_cast<__half2*>(&hi));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
+}
+
+// Converts row r (0..63) of one fp8 code tile (128 B rows, SWIZZLE_128B) into
+// the two 64-element halves of the dtype tile at dst (SWIZZLE_128B), each
+// value times `scale`.
+template <typename T>
+__device__ __forceinline__ void dec8_convert_row(const uint8_t* codes, uint8_t* dst, int r,
+                                                 float scale) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds d = 16c .. 16c + 15
+    const uint4 w = *reinterpret_cast<const uint4*>(codes + r * 128 + ((c ^ (r & 7)) * 16));
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float f[4];
+      e4m3x4_to_f32(ws[k], f);
+      out[2 * k] = DT<T>::from_f2(__fmul_rn(f[0], scale), __fmul_rn(f[1], scale));
+      out[2 * k + 1] = DT<T>::from_f2(__fmul_rn(f[2], scale), __fmul_rn(f[3], scale));
+    }
+    uint8_t* half = dst + (c >> 2) * kDecHalfBytes + r * 128;
+    const int j0 = (2 * c) & 7, j1 = (2 * c + 1) & 7;
+    *reinterpret_cast<uint4*>(half + ((j0 ^ (r & 7)) * 16)) =
+        make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(half + ((j1 ^ (r & 7)) * 16)) =
+        make_uint4(out[4], out[5], out[6], out[7]);
+  }
+}
+
+template <typename T, bool kHi, bool kFp8>
+__global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
+  constexpr int kStages = kFp8 ? kDec8Stages : kDecStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
-  uint64_t* empty = full + kDecStages;
-  float* red = reinterpret_cast<float*>(empty + kDecStages);  // [warp][m|l][16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      smem + (kFp8 ? kDec8OffBars : kDecStages * kDecStageBytes));
+  uint64_t* empty = full + kStages;
+  uint64_t* code_full = empty + kStages;        // fp8: the stage's codes landed
+  uint64_t* code_empty = code_full + kStages;   // fp8: the stage's codes converted
+  float* red = reinterpret_cast<float*>(kFp8 ? code_empty + kStages : empty + kStages);
+  int64_t* stage_row = reinterpret_cast<int64_t*>(smem + kDec8OffRow);  // fp8: first row
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
 #pragma unroll
-    for (int s = 0; s < kDecStages; ++s) {
-      mbar_init(&full[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], kFp8 ? kDec8ConvWarps : 1);
       mbar_init(&empty[s], kDecComputeWarps);
+      if (kFp8) {
+        mbar_init(&code_full[s], 1);
+        mbar_init(&code_empty[s], kDec8ConvWarps);
+      }
     }
     fence_mbar_init();
   }
@@ -106,13 +177,40 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   if (k_len <= 0 && threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
   __syncthreads();
 
+  if (kFp8 && warp > kDecComputeWarps) {
+    // ------------------------------ fp8 converters ------------------------------
+    const int r = (warp - kDecComputeWarps - 1) * 32 + lane;  // tile row 0..63
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % kStages;
+      const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+      if (!mbar_wait(&code_full[s], ph, p.err)) break;
+      if (it >= kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
+      // the row's scales: [page][kv head][row in page]
+      const int64_t row = stage_row[s] + r;
+      const int64_t page = row / p.page_size;
+      const int64_t si = (page * p.num_kv_heads + kvh) * p.page_size + row % p.page_size;
+      const float ks = __ldg(p.k_scale + si), vs = __ldg(p.v_scale + si);
+      const uint8_t* codes = smem + kDec8OffCodes + s * kDec8CodeStage;
+      uint8_t* dst = smem + s * kDecStageBytes;
+      dec8_convert_row<T>(codes, dst, r, ks);
+      dec8_convert_row<T>(codes + kDec8CodeTile, dst + kDecTileBytes, r, vs);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&code_empty[s]);
+        mbar_arrive(&full[s]);
+      }
+    }
+    return;
+  }
+
   if (warp == kDecComputeWarps) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       for (int it = 0; it < ntiles; ++it) {
-        const int s = it % kDecStages;
-        const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
-        if (it >= kDecStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
+        const int s = it % kStages;
+        const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+        uint64_t* reuse = kFp8 ? &code_empty[s] : &empty[s];
+        if (it >= kStages && !mbar_wait(reuse, ph ^ 1u, p.err)) break;
         const int j0 = tok_begin + it * kDecTile;
         int64_t row;
         if (it == 0 && p.block_tables) {
@@ -126,7 +224,15 @@ __global__ void __launch_bounds__(kDecThreads, 2)
           row = dec_tile_row(p.block_tables, p.bt_stride, p.num_blocks, p.page_size, p.cu_k, b,
                              j0, p.err);
         }
-        dec_load_stage(smem + s * kDecStageBytes, &full[s], &tmap_k, &tmap_v, kvh, row);
+        if (kFp8) {
+          uint8_t* codes = smem + kDec8OffCodes + s * kDec8CodeStage;
+          stage_row[s] = row;  // published by the arrive below
+          mbar_arrive_expect_tx(&code_full[s], kDec8CodeStage);
+          tma_load_3d(codes, &tmap_k, &code_full[s], 0, kvh, (int)row);
+          tma_load_3d(codes + kDec8CodeTile, &tmap_v, &code_full[s], 0, kvh, (int)row);
+        } else {
+          dec_load_stage(smem + s * kDecStageBytes, &full[s], &tmap_k, &tmap_v, kvh, row);
+        }
       }
     }
     return;
@@ -144,8 +250,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   st.reset();
 
   for (int it = 0; it < ntiles; ++it) {
-    const int s = it % kDecStages;
-    const uint32_t ph = (uint32_t)(it / kDecStages) & 1u;
+    const int s = it % kStages;
+    const uint32_t ph = (uint32_t)(it / kStages) & 1u;
     if (!mbar_wait(&full[s], ph, p.err)) break;
     const uint32_t kbase = smem_u32(smem + s * kDecStageBytes);
     const int valid = tok_end - (tok_begin + it * kDecTile + warp * 16);  // keys of this slice
@@ -299,16 +405,37 @@ static int launch_combine(void (*kern)(DecodeParams), const DecodeParams& p, con
                     p);
 }
 
+template <typename T, bool kFp8>
+static int launch_decode_grid(bool hi, dim3 grid, const CUtensorMap& mk, const CUtensorMap& mv,
+                              const DecodeParams& p, cudaStream_t stream) {
+  auto kern = hi ? paged_decode_kernel<T, true, kFp8> : paged_decode_kernel<T, false, kFp8>;
+  constexpr int smem = kFp8 ? kDec8SmemBytes : kDecSmemBytes;
+  constexpr int threads = kFp8 ? kDec8Threads : kDecThreads;
+  static unsigned long long attr_done[2] = {0, 0};  // per instantiation and kHi
+  int rc = ensure_smem_attr((const void*)kern, smem, &attr_done[hi]);
+  if (!rc)
+    rc = launch_pdl(kern, grid, dim3(threads), smem, stream, "paged decode launch", mk, mv, p);
+  return rc;
+}
+
 int launch_paged_decode(const AttnArgs& a) {
   int chunk, splits;
   decode_plan(a.num_seqs, a.hkv, a.max_k, &chunk, &splits);
   const int64_t rows = a.block_tables ? a.num_blocks * a.page : a.num_blocks;
+  const bool fp8 = a.k_scale != nullptr;
   CUtensorMap mk, mv;
-  int rc = encode_kv_tensor_map(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64, kDecTile,
-                                true);
-  if (rc) return rc;
-  rc = encode_kv_tensor_map(&mv, a.v_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64, kDecTile,
-                            true);
+  int rc;
+  if (fp8) {  // paged only; rows of Hkv x 128 one-byte codes
+    rc = encode_kv_tensor_map_u8(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride, kDecTile);
+    if (!rc)
+      rc = encode_kv_tensor_map_u8(&mv, a.v_cache, kDecD, a.hkv, rows, a.kv_stride, kDecTile);
+  } else {
+    rc = encode_kv_tensor_map(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64, kDecTile,
+                              true);
+    if (!rc)
+      rc = encode_kv_tensor_map(&mv, a.v_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64,
+                                kDecTile, true);
+  }
   if (rc) return rc;
   DecodeParams p;
   p.q = a.q;
@@ -330,6 +457,9 @@ int launch_paged_decode(const AttnArgs& a) {
   p.ws_o = nullptr;
   p.ws_lse = nullptr;
   p.err = device_error_word();
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
+  p.num_kv_heads = a.hkv;
   if (splits > 1) {
     const size_t n = (size_t)a.num_seqs * splits * a.hq;
     p.ws_o = reinterpret_cast<float*>(a.ws);
@@ -339,19 +469,12 @@ int launch_paged_decode(const AttnArgs& a) {
   // group sizes up to 8 leave fragment rows 8..15 as padding (kHi = false)
   const bool hi = p.group > 8;
   if (a.dtype == NVKV_DTYPE_BF16) {
-    auto kern = hi ? paged_decode_kernel<__nv_bfloat16, true>
-                   : paged_decode_kernel<__nv_bfloat16, false>;
-    static unsigned long long attr_done[2] = {0, 0};
-    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done[hi]);
-    if (!rc) rc = launch_pdl(kern, grid, dim3(kDecThreads), kDecSmemBytes, a.stream,
-                             "paged decode launch", mk, mv, p);
+    rc = fp8 ? launch_decode_grid<__nv_bfloat16, true>(hi, grid, mk, mv, p, a.stream)
+             : launch_decode_grid<__nv_bfloat16, false>(hi, grid, mk, mv, p, a.stream);
     if (!rc && splits > 1) rc = launch_combine(decode_combine_kernel<__nv_bfloat16>, p, a);
   } else {
-    auto kern = hi ? paged_decode_kernel<__half, true> : paged_decode_kernel<__half, false>;
-    static unsigned long long attr_done[2] = {0, 0};
-    rc = ensure_smem_attr((const void*)kern, kDecSmemBytes, &attr_done[hi]);
-    if (!rc) rc = launch_pdl(kern, grid, dim3(kDecThreads), kDecSmemBytes, a.stream,
-                             "paged decode launch", mk, mv, p);
+    rc = fp8 ? launch_decode_grid<__half, true>(hi, grid, mk, mv, p, a.stream)
+             : launch_decode_grid<__half, false>(hi, grid, mk, mv, p, a.stream);
     if (!rc && splits > 1) rc = launch_combine(decode_combine_kernel<__half>, p, a);
   }
   return rc;

@@ -79,6 +79,13 @@ SIGNATURES = {
     "nvkv_paged_attention_noalloc": [_p, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64,
                                      _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
                                      _p],
+    "nvkv_store_kvcache_fp8": [_p, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i64, _i64, _i64,
+                               _i32, _i32, _p],
+    "nvkv_paged_attention_fp8_workspace_size": [_i32, _i32, _i32, _i32, _i32, _i32, _i64,
+                                                ctypes.POINTER(_sz)],
+    "nvkv_paged_attention_fp8": [_p, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64,
+                                 _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i64, _p,
+                                 _sz, _i32, _p],
     "nvkv_rms_norm": [_p, _i64, _p, _i64, _p, _f32, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_silu_and_mul": [_p, _i64, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_decode_advance": [_i32, _i32, _p, _p, _i64, _i64, _p, _p, _p, _p, _p],

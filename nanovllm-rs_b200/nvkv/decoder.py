@@ -132,6 +132,7 @@ class Step:
     last_idx: torch.Tensor      # [B] int64: row of each sequence's last token
     max_seqlen_q: int
     max_seqlen_k: int
+    prompt_kv_tokens: int = 0   # fp8 pool: >= sum of k_len over the q_len > 1 sequences
 
 
 class Qwen3TP:
@@ -194,6 +195,9 @@ class Qwen3TP:
         del emb, lm
         self.k_caches: List[torch.Tensor] = []
         self.v_caches: List[torch.Tensor] = []
+        self.k_scales: List[torch.Tensor] = []  # fp8 pool only: [Nb, Hkv, P] f32
+        self.v_scales: List[torch.Tensor] = []
+        self.kv_fp8 = False
         self._bufs = {}
         self.comm = None
         self._own_comm = False
@@ -213,12 +217,33 @@ class Qwen3TP:
 
     # ---- KV pool (model_runner.rs:286-303): per layer [Nb, P, Hkv/tp, D] ----
     def allocate_kv_cache(self, num_blocks: int, block_size: int = 256, fill_random: bool = False,
-                          seed: int = 1) -> None:
+                          seed: int = 1, kv_fp8: bool = False) -> None:
+        """kv_fp8: the optional e4m3 pool (codes [Nb, P, Hkv, D] uint8 + f32 row
+        scales [Nb, Hkv, P], nvkv_store_kvcache_fp8 / nvkv_paged_attention_fp8)
+        instead of the model dtype.  fill_random fills the pool with random
+        rows (through the fp8 store for an fp8 pool)."""
         shape = (num_blocks, block_size, self.hkv, self.cfg.head_dim)
-        self.k_caches, self.v_caches = [], []
+        self.k_caches, self.v_caches, self.k_scales, self.v_scales = [], [], [], []
+        self.kv_fp8 = kv_fp8
         g = torch.Generator(device=self.device).manual_seed(seed * 7919 + self.rank)
+        slots = torch.arange(num_blocks * block_size, device=self.device) if kv_fp8 else None
         for _ in range(self.cfg.num_hidden_layers):
-            if fill_random:
+            if kv_fp8:
+                k = torch.zeros(shape, device=self.device, dtype=torch.uint8)
+                v = torch.zeros_like(k)
+                ks = torch.zeros(num_blocks, self.hkv, block_size, device=self.device)
+                vs = torch.zeros_like(ks)
+                if fill_random:
+                    for lo in range(0, num_blocks, 64):  # bounded temporaries
+                        n = min(64, num_blocks - lo)
+                        rk = torch.randn((n * block_size,) + shape[2:], generator=g,
+                                         device=self.device, dtype=self.dtype)
+                        rv = torch.randn_like(rk)
+                        ops.store_kvcache_fp8(rk, rv, k, v, ks, vs,
+                                              slots[lo * block_size:(lo + n) * block_size])
+                self.k_scales.append(ks)
+                self.v_scales.append(vs)
+            elif fill_random:
                 k = torch.randn(shape, generator=g, device=self.device, dtype=self.dtype)
                 v = torch.randn(shape, generator=g, device=self.device, dtype=self.dtype)
             else:
@@ -226,6 +251,43 @@ class Qwen3TP:
                 v = torch.zeros(shape, device=self.device, dtype=self.dtype)
             self.k_caches.append(k)
             self.v_caches.append(v)
+
+    def _attend(self, li: int, qkv: torch.Tensor, st: "Step", q_buf, o_buf, ws) -> None:
+        """One layer's attention hot path: the q/k-norm + RoPE prologue with the
+        KV-cache store, then paged attention (qwen3.rs:128-145), over the
+        model-dtype pool (the store fused into the prologue) or the fp8 pool
+        (prologue, fp8 store, fp8 attention)."""
+        cfg, D, eps = self.cfg, self.cfg.head_dim, self.cfg.rms_norm_eps
+        L = self.layers[li]
+        if not self.kv_fp8:
+            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"], eps,
+                            cfg.rope_theta, cfg.max_position_embeddings, D,
+                            k_cache=self.k_caches[li], v_cache=self.v_caches[li],
+                            slot_mapping=st.slot_mapping, q_out=q_buf)
+            ops.paged_attention(q_buf, self.k_caches[li], self.v_caches[li], st.cu_seqlens_q,
+                                st.cu_seqlens_k, st.block_tables, st.max_seqlen_q,
+                                st.max_seqlen_k, self.scale, out=o_buf, workspace=ws)
+            return
+        _, k_out, v_out = ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"],
+                                          L["kn"], eps, cfg.rope_theta,
+                                          cfg.max_position_embeddings, D, want_kv=True,
+                                          q_out=q_buf)
+        ops.store_kvcache_fp8(k_out, v_out, self.k_caches[li], self.v_caches[li],
+                              self.k_scales[li], self.v_scales[li], st.slot_mapping)
+        ops.paged_attention_fp8(q_buf, self.k_caches[li], self.v_caches[li], self.k_scales[li],
+                                self.v_scales[li], st.cu_seqlens_q, st.cu_seqlens_k,
+                                st.block_tables, st.max_seqlen_q, st.max_seqlen_k, self.scale,
+                                prompt_kv_tokens=st.prompt_kv_tokens, out=o_buf, workspace=ws)
+
+    def _ws(self, st: "Step") -> torch.Tensor:
+        B = st.cu_seqlens_q.numel() - 1
+        if self.kv_fp8:
+            n = ops.workspace_size_fp8(B, self.hq, self.hkv, st.max_seqlen_q, st.max_seqlen_k,
+                                       st.prompt_kv_tokens, self.cfg.head_dim)
+        else:
+            n = ops.workspace_size(B, self.hq, self.hkv, st.max_seqlen_q, st.max_seqlen_k,
+                                   self.cfg.head_dim)
+        return self._buf("ws", (max(n, 16),), torch.uint8)
 
     def _buf(self, name, shape, dtype=None):
         b = self._bufs.get(name)
@@ -269,9 +331,7 @@ class Qwen3TP:
             h = torch.nn.functional.embedding(st.input_ids, self.embed)
         q_buf = self._buf("q", (T, self.hq, D))
         o_buf = self._buf("o", (T, self.hq, D))
-        ws_n = ops.workspace_size(st.cu_seqlens_q.numel() - 1, self.hq, self.hkv, st.max_seqlen_q,
-                                  st.max_seqlen_k, D)
-        ws = self._buf("ws", (max(ws_n, 16),), torch.uint8)
+        ws = self._ws(st)
         xb = self._buf("x", (T, cfg.hidden_size))
         actb = self._buf("act", (T, self.ffn))
         eps = cfg.rms_norm_eps
@@ -284,13 +344,7 @@ class Qwen3TP:
             else:
                 x = ops.rms_norm(h, L["ln1"], eps, residual=residual, out=xb)
             qkv = torch.matmul(x, L["qkv"].t())
-            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"], eps,
-                            cfg.rope_theta, cfg.max_position_embeddings, D,
-                            k_cache=self.k_caches[li], v_cache=self.v_caches[li],
-                            slot_mapping=st.slot_mapping, q_out=q_buf)
-            ops.paged_attention(q_buf, self.k_caches[li], self.v_caches[li], st.cu_seqlens_q,
-                                st.cu_seqlens_k, st.block_tables, st.max_seqlen_q,
-                                st.max_seqlen_k, self.scale, out=o_buf, workspace=ws)
+            self._attend(li, qkv, st, q_buf, o_buf, ws)
             a = self._all_reduce(torch.matmul(o_buf.view(T, -1), L["o"].t()))
             x = ops.rms_norm(a, L["ln2"], eps, residual=residual, out=xb)
             gu = torch.matmul(x, L["gate_up"].t())
@@ -316,9 +370,7 @@ class Qwen3TP:
         part = self.comm.input(T, H, self.dtype)
         q_buf = self._buf("q", (T, self.hq, D))
         o_buf = self._buf("o", (T, self.hq, D))
-        ws_n = ops.workspace_size(st.cu_seqlens_q.numel() - 1, self.hq, self.hkv, st.max_seqlen_q,
-                                  st.max_seqlen_k, D)
-        ws = self._buf("ws", (max(ws_n, 16),), torch.uint8)
+        ws = self._ws(st)
         xb = self._buf("x", (T, H))
         res = self._buf("res", (T, H))
         actb = self._buf("act", (T, self.ffn))
@@ -331,13 +383,7 @@ class Qwen3TP:
         self.comm.allreduce_rms_norm(T, H, res, self.layers[0]["ln1"], eps, xb, init=True)
         for li, L in enumerate(self.layers):
             qkv = torch.matmul(xb, L["qkv"].t())
-            ops.qknorm_rope(qkv, st.positions, self.hq, self.hkv, L["qn"], L["kn"], eps,
-                            cfg.rope_theta, cfg.max_position_embeddings, D,
-                            k_cache=self.k_caches[li], v_cache=self.v_caches[li],
-                            slot_mapping=st.slot_mapping, q_out=q_buf)
-            ops.paged_attention(q_buf, self.k_caches[li], self.v_caches[li], st.cu_seqlens_q,
-                                st.cu_seqlens_k, st.block_tables, st.max_seqlen_q,
-                                st.max_seqlen_k, self.scale, out=o_buf, workspace=ws)
+            self._attend(li, qkv, st, q_buf, o_buf, ws)
             torch.matmul(o_buf.view(T, -1), L["o"].t(), out=part)
             self.comm.allreduce_rms_norm(T, H, res, L["ln2"], eps, xb)
             gu = torch.matmul(xb, L["gate_up"].t())
@@ -353,10 +399,13 @@ class Qwen3TP:
         (each fused with the all-reduce before it on the peer route), SiLU*mul,
         the prologue, the decode kernel, the combine kernel when the split-KV
         plan splits, and the prefill work plan + prefill kernel when
-        max_seqlen_q > 1; plus the final norm (on the peer route: the
+        max_seqlen_q > 1 (with an fp8 pool also its store and, for prompts,
+        the dequantisation); plus the final norm (on the peer route: the
         embedding's fused call, the final norm being fused into the last
         layer's)."""
         B = st.cu_seqlens_q.numel() - 1
         split = ops.workspace_size(B, self.hq, self.hkv, 1, st.max_seqlen_k) > 0
         per = 5 + (1 if split else 0) + (2 if st.max_seqlen_q > 1 else 0)
+        if self.kv_fp8:  # + the fp8 store; prompts: + row offsets and dequantisation
+            per += 1 + (2 if st.max_seqlen_q > 1 else 0)
         return per * self.cfg.num_hidden_layers + 1

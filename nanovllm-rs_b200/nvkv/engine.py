@@ -210,9 +210,13 @@ class Engine:
         cu_q = d["cu_q"][:B + 1]
         last = cu_q.index_select(0, d["need"][:n_need] + 1).long() - 1
         self._n_need = n_need
+        prompt_rows = 0
+        if sizes.max_seqlen_q > 1:  # the fp8 pool dequantises the prompts' keys
+            ql = np.diff(h["cu_q"][:B + 1].numpy())
+            prompt_rows = int(h["ctx"][:B].numpy()[ql > 1].sum())
         return Step(d["ids"][:T], d["pos"][:T], d["slots"][:T], cu_q, d["cu_k"][:B + 1],
                     d["bt"][:B * W].view(B, W), last, int(sizes.max_seqlen_q),
-                    int(sizes.max_seqlen_k))
+                    int(sizes.max_seqlen_k), prompt_rows)
 
     def step(self) -> int:
         """One engine step; returns the number of tokens sampled."""

@@ -159,6 +159,72 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     return out
 
 
+def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                      v_cache: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
+                      slot_mapping: torch.Tensor) -> None:
+    """The fp8 (e4m3) pool's store (nvkv_store_kvcache_fp8): key/value
+    [T, Hkv, 128] bf16/f16 rows quantised into k_cache/v_cache
+    [Nb, P, Hkv, 128] uint8 with one f32 scale per row in k_scale/v_scale
+    [Nb, Hkv, P]."""
+    _need(key.is_cuda and k_cache.is_cuda, "store_kvcache_fp8 is cuda-only")
+    _need(k_cache.dtype == torch.uint8 and v_cache.dtype == torch.uint8, "fp8 caches are uint8")
+    _need(k_scale.dtype == torch.float32 and v_scale.dtype == torch.float32, "scales are f32")
+    _need(k_cache.dim() == 4 and k_cache.is_contiguous() and v_cache.is_contiguous() and
+          k_scale.is_contiguous() and v_scale.is_contiguous(), "contiguous pool")
+    Nb, P, hkv, d = k_cache.shape
+    _need(tuple(k_scale.shape) == (Nb, hkv, P) == tuple(v_scale.shape), "scales [Nb, Hkv, P]")
+    _need(key.dim() == 3 and key.shape[1:] == (hkv, d) and value.shape == key.shape, "key shape")
+    _need(slot_mapping.dtype == torch.int64 and slot_mapping.is_contiguous(), "slot_mapping")
+    T = key.size(0)
+    _need(_row_view_ok(key) and _row_view_ok(value), "key/value rows must be dense")
+    check(lib.nvkv_store_kvcache_fp8(_ptr(key), _ptr(value), _ptr(k_cache), _ptr(v_cache),
+                                     _ptr(k_scale), _ptr(v_scale), _ptr(slot_mapping), T, hkv, d,
+                                     key.stride(0) if T > 1 else hkv * d,
+                                     value.stride(0) if T > 1 else hkv * d, Nb, P, _dtype(key),
+                                     _stream()))
+
+
+def workspace_size_fp8(num_seqs: int, num_q_heads: int, num_kv_heads: int, max_seqlen_q: int,
+                       max_seqlen_k: int, prompt_kv_tokens: int, head_dim: int = 128) -> int:
+    n = ctypes.c_size_t(0)
+    check(lib.nvkv_paged_attention_fp8_workspace_size(num_seqs, num_q_heads, num_kv_heads,
+                                                      head_dim, max_seqlen_q, max_seqlen_k,
+                                                      int(prompt_kv_tokens), ctypes.byref(n)))
+    return n.value
+
+
+def paged_attention_fp8(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                        k_scale: torch.Tensor, v_scale: torch.Tensor,
+                        cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor,
+                        block_tables: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int,
+                        softmax_scale: float, prompt_kv_tokens: int = 0, causal: bool = True,
+                        out: Optional[torch.Tensor] = None,
+                        workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """paged_attention over the fp8 (e4m3) pool (nvkv_paged_attention_fp8).
+    prompt_kv_tokens: at least the sum of k_len over the q_len > 1 sequences."""
+    _need(q.is_cuda and q.dim() == 3 and _row_view_ok(q), "q must be [T, Hq, D] on cuda")
+    _need(k_cache.dtype == torch.uint8 and k_cache.dim() == 4 and k_cache.is_contiguous() and
+          v_cache.is_contiguous(), "fp8 caches: contiguous uint8 [Nb, P, Hkv, D]")
+    _need(block_tables.dtype in (torch.int32, torch.uint32) and block_tables.is_contiguous(),
+          "block_tables must be contiguous 32-bit")
+    T, hq, d = q.shape
+    nb, page, hkv = k_cache.size(0), k_cache.size(1), k_cache.size(2)
+    B = cu_seqlens_q.numel() - 1
+    if out is None:
+        out = torch.empty(T, hq, d, device=q.device, dtype=q.dtype)
+    need = workspace_size_fp8(B, hq, hkv, max_seqlen_q, max_seqlen_k, prompt_kv_tokens, d)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, device=q.device, dtype=torch.uint8)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib.nvkv_paged_attention_fp8(
+        _ptr(q), q.stride(0) if T > 1 else hq * d, T, _ptr(k_cache), _ptr(v_cache),
+        _ptr(k_scale), _ptr(v_scale), nb, _ptr(out), _ptr(cu_seqlens_q), _ptr(cu_seqlens_k),
+        _ptr(block_tables), block_tables.size(1), B, int(max_seqlen_q), int(max_seqlen_k), hq, hkv,
+        d, page, float(softmax_scale), 1 if causal else 0, int(prompt_kv_tokens),
+        _ptr(workspace), ws_bytes, _dtype(q), _stream()))
+    return out
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
              residual: Optional[torch.Tensor] = None,
              out: Optional[torch.Tensor] = None) -> torch.Tensor:

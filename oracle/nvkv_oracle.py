@@ -419,3 +419,89 @@ def repro_inputs(layer: int):
     v_new = repro_mk(sd(1.7), 1, REPRO_N_KV_HEADS)
     q_new = repro_mk(sd(2.1), 1, REPRO_N_HEADS)
     return k_prior, v_prior, k_new, v_new, q_new
+
+
+# --------------------------------------------------------------------------
+# f4: FP8 (e4m3) KV-cache format -- no counterpart in the reference, whose
+# pool is in the model dtype (engine/model_runner.rs:286-303).  Restated here
+# as the checker of nvkv's optional fp8 pool: each (token, kv head) row of D
+# values is stored as e4m3 codes with its own f32 scale,
+#   scale = amax / 448,  code = e4m3_rn_satfinite(x * (448 / amax))
+# (amax = max |x| over the row; an all-zero row gets scale 0 and zero codes),
+# and read back as code_value * scale.  Scales are laid out [Nb, Hkv, P].
+# --------------------------------------------------------------------------
+
+E4M3_MAX = 448.0
+
+
+def _e4m3_table():
+    """Value of every e4m3 code (OCP E4M3FN: bias 7, no infinities, codes
+    0x7F / 0xFF are NaN)."""
+    vals = np.zeros(256, np.float64)
+    for c in range(256):
+        s = -1.0 if c & 0x80 else 1.0
+        e = (c >> 3) & 0xF
+        m = c & 0x7
+        if e == 0xF and m == 0x7:
+            vals[c] = np.nan
+        elif e == 0:
+            vals[c] = s * m * 2.0 ** -9
+        else:
+            vals[c] = s * (1 + m / 8.0) * 2.0 ** (e - 7)
+    return vals
+
+
+E4M3_VALUES = _e4m3_table()
+
+
+def e4m3_encode(x) -> np.ndarray:
+    """float32 -> e4m3 codes (uint8): round to nearest, ties to the even code,
+    magnitudes above 448 saturate to 448 (the satfinite conversion)."""
+    x = np.asarray(x, np.float32).astype(np.float64)
+    a = np.minimum(np.abs(x), E4M3_MAX)
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -9)))
+    e = np.clip(e, -6, 8)  # exponent of the binade; below 2^-6 the subnormal step 2^-9
+    q = 2.0 ** (e - 3)
+    mag = np.rint(a / q) * q  # exact in f64; rint rounds half to even
+    mag = np.minimum(mag, E4M3_MAX)
+    pos = E4M3_VALUES[:0x7F]  # the finite non-negative codes, increasing
+    code = np.searchsorted(pos, mag).astype(np.uint8)
+    return np.where(x < 0, code | 0x80, code).astype(np.uint8)
+
+
+def e4m3_decode(code) -> np.ndarray:
+    return E4M3_VALUES[np.asarray(code, np.uint8)].astype(np.float32)
+
+
+def quantize_rows_fp8(x):
+    """[..., D] float32 rows -> (codes uint8 [..., D], scales float32 [...]),
+    with the f32 arithmetic of nvkv's store (division and product rounded to
+    nearest)."""
+    x = np.asarray(x, np.float32)
+    amax = np.max(np.abs(x), axis=-1)
+    with np.errstate(divide="ignore"):
+        scale = (amax / np.float32(E4M3_MAX)).astype(np.float32)
+        inv = np.where(amax > 0, np.float32(E4M3_MAX) / amax, np.float32(0)).astype(np.float32)
+    codes = e4m3_encode((x * inv[..., None]).astype(np.float32))
+    return codes, scale
+
+
+def store_kvcache_fp8(key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping) -> None:
+    """The fp8 pool's store: caches [Nb, P, Hkv, D] uint8, scales [Nb, Hkv, P]
+    float32; row t of key/value ([T, Hkv, D], float32 values) goes to slot
+    slot_mapping[t] (negative slots skipped)."""
+    P = k_cache.shape[1]
+    slots = np.asarray(slot_mapping, np.int64)
+    for cache, scales, src in ((k_cache, k_scale, key), (v_cache, v_scale, value)):
+        codes, sc = quantize_rows_fp8(np.asarray(src, np.float32))
+        for t, s in enumerate(slots):
+            if s < 0:
+                continue
+            cache[s // P, s % P] = codes[t]
+            scales[s // P, :, s % P] = sc[t]
+
+
+def dequantize_pages_fp8(cache, scales) -> np.ndarray:
+    """[Nb, P, Hkv, D] codes + [Nb, Hkv, P] scales -> float32 values."""
+    vals = e4m3_decode(cache)
+    return (vals * np.transpose(scales, (0, 2, 1))[..., None]).astype(np.float32)
