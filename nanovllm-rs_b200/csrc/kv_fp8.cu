@@ -358,12 +358,12 @@ extern "C" int nvkv_paged_attention_fp8(
   a.stream = reinterpret_cast<cudaStream_t>(stream);
   a.k_scale = k_scale;
   a.v_scale = v_scale;
-  rc = launch_paged_decode(a);  // q_len == 1 rows, straight from the fp8 pool
-  if (rc || max_seqlen_q <= 1) return rc;
-  if (prompt_kv_tokens == 0)
+  if (max_seqlen_q > 1 && prompt_kv_tokens == 0)
     return set_error(NVKV_ERR_INVALID_ARG,
                      "paged_attention_fp8: max_seqlen_q > 1 needs prompt_kv_tokens >= the "
                      "prompts' total k_len");
+  rc = launch_paged_decode(a);  // q_len == 1 rows, straight from the fp8 pool
+  if (rc || max_seqlen_q <= 1) return rc;
   // q_len > 1 rows: dequantise the prompts' keys, then the contiguous prefill
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint32_t* cu_kd = reinterpret_cast<uint32_t*>(ws + L.cu_kd);
