@@ -72,7 +72,7 @@ class Engine:
 
     def __init__(self, model, num_blocks: int, block_size: int = 256, max_num_seqs: int = 512,
                  max_num_batched_tokens: int = 16384, max_model_len: int = 40960,
-                 eos: int = -1):
+                 eos: int = -1, cuda_graphs: bool = True):
         self.model = model
         self.block_size = block_size
         self.max_num_seqs = max_num_seqs
@@ -100,8 +100,20 @@ class Engine:
         self.d = {k: torch.zeros(v.numel(), dtype=v.dtype, device=dev) for k, v in self.h.items()}
         self.tok_h = torch.zeros(B, dtype=torch.int64, **pin)
         self.stats = []  # per step: (prompt tokens, decode tokens, seconds)
+        # pure decode steps replay a CUDA graph per (batch size, context bucket);
+        # a key is captured when it repeats on consecutive steps (config-4-like
+        # runs decode hundreds of steps at one batch size)
+        self.cuda_graphs = cuda_graphs and self._cuda
+        self._graphs: Dict[tuple, tuple] = {}
+        self._last_key = None
+        self.bt_g = torch.zeros(B * self._w, dtype=torch.int32, **pin)
+        self.d_bt_g = torch.zeros(B * self._w, dtype=torch.int32, device=dev)
+        self.graph_steps = 0
 
     def close(self) -> None:
+        for g, _ in self._graphs.values():  # graphs may hold collectives: drop them first
+            g.reset()
+        self._graphs.clear()
         self.bm.close()
 
     # ---- requests ----------------------------------------------------------
@@ -211,6 +223,9 @@ class Engine:
         last = cu_q.index_select(0, d["need"][:n_need] + 1).long() - 1
         self._n_need = n_need
         prompt_rows = 0
+        self._decode_only = (sizes.max_seqlen_q == 1 and n_need == B and
+                             bool(sizes.has_block_tables))
+        self._B, self._W, self._max_k = B, W, int(sizes.max_seqlen_k)
         if sizes.max_seqlen_q > 1:  # the fp8 pool dequantises the prompts' keys
             ql = np.diff(h["cu_q"][:B + 1].numpy())
             prompt_rows = int(h["ctx"][:B].numpy()[ql > 1].sum())
@@ -225,7 +240,9 @@ class Engine:
         prompt_tok = sum(int(s.c.num_new_tokens) for s in sched if s.c.num_new_tokens > 1)
         decode_tok = sum(1 for s in sched if s.c.num_new_tokens == 1)
         st = self._prepare(sched)
-        tok = self.model.greedy(st)
+        tok = self._decode_graph(st) if self.cuda_graphs and self._decode_only else None
+        if tok is None:
+            tok = self.model.greedy(st)
         n = self._n_need
         self.tok_h[:n].copy_(tok[:n], non_blocking=self._cuda)
         if self._cuda:
@@ -252,6 +269,52 @@ class Engine:
                 s.c.num_new_tokens = 0
         self.stats.append((prompt_tok, decode_tok, time.perf_counter() - t0))
         return n
+
+    def _decode_graph(self, st: Step) -> Optional[torch.Tensor]:
+        """A pure decode step through a captured CUDA graph, or None (then the
+        step runs eagerly).  The graph's step has fixed shapes: the batch size,
+        max_seqlen_k rounded up to a multiple of 1024 (the kernels take it as a
+        bound) and block tables padded to that many pages in a fixed buffer;
+        the step's own metadata is copied into the same device buffers first."""
+        B, P = self._B, self.block_size
+        bucket = -(-self._max_k // 1024) * 1024
+        key = (B, bucket)
+        g = self._graphs.get(key)
+        if g is None and (self._last_key != key or len(self._graphs) >= 8):
+            self._last_key = key
+            return None
+        self._last_key = key
+        Wg = -(-bucket // P)
+        bt = self.bt_g[:B * Wg].view(B, Wg).numpy()
+        bt.fill(0)
+        bt[:, :self._W] = self.h["bt"][:B * self._W].view(B, self._W).numpy()
+        self.d_bt_g[:B * Wg].copy_(self.bt_g[:B * Wg], non_blocking=True)
+        d = self.d
+        stg = Step(d["ids"][:B], d["pos"][:B], d["slots"][:B], d["cu_q"][:B + 1],
+                   d["cu_k"][:B + 1], self.d_bt_g[:B * Wg].view(B, Wg), st.last_idx, 1, bucket, 0)
+        if g is None:  # capture: one eager warm-up of these shapes, then the graph
+            self.model.greedy(stg)
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.model.greedy(stg)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            last = d["need"][:B]
+            # the model's scratch buffers of this graph come from the graph's
+            # own memory pool, so later eager steps that reallocate them (other
+            # shapes) never hand the graph's memory to anything else
+            saved, self.model._bufs = self.model._bufs, {}
+            try:
+                with torch.cuda.graph(graph):
+                    stg.last_idx = d["cu_q"].index_select(0, last + 1).long() - 1
+                    out = self.model.greedy(stg)
+            finally:
+                self.model._bufs = saved
+            g = self._graphs[key] = (graph, out)
+        g[0].replay()
+        self.graph_steps += 1
+        return g[1]
 
     def generate(self, prompts, max_tokens: int, ignore_eos: bool = True) -> List[List[int]]:
         """LLMEngine::generate: every prompt to completion; the completions in
