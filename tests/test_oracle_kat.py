@@ -207,3 +207,47 @@ def test_reference_arm_imports_no_native_library():
             "assert not bad, bad" % (root, os.path.join(root, "nanovllm-rs_b200"),
                                      os.path.join(root, "oracle")))
     subprocess.run([sys.executable, "-c", code], check=True, cwd=root)
+
+
+def test_e4m3_encoder_every_code_and_midpoint():
+    """The oracle's e4m3 encoder (checker of the fp8 pool's store): every
+    finite code round-trips, every midpoint between neighbours goes to the
+    code with the even mantissa, magnitudes above 448 saturate, signs are
+    kept, and values below half the smallest subnormal go to zero."""
+    vals = O.E4M3_VALUES
+    pos = vals[:0x7F]
+    codes = np.arange(0x7F, dtype=np.uint8)
+    assert np.array_equal(O.e4m3_encode(pos.astype(np.float32)), codes)
+    assert np.array_equal(O.e4m3_encode(-pos[1:].astype(np.float32)), codes[1:] | 0x80)
+    mids = ((pos[:-1] + pos[1:]) / 2).astype(np.float32)
+    got = O.e4m3_encode(mids)
+    even = np.where(codes[:-1] % 2 == 0, codes[:-1], codes[1:])
+    assert np.array_equal(got, even)
+    assert list(O.e4m3_decode(O.e4m3_encode(np.array([449, 1e30, -500], np.float32)))) == [
+        448, 448, -448]
+    assert O.e4m3_encode(np.array([2.0 ** -11], np.float32))[0] == 0
+
+
+def test_fp8_row_quantisation_round_trip():
+    """quantize_rows_fp8: scale = amax / 448, codes within half an e4m3 step of
+    x / scale, a zero row gives scale 0 and zero codes; the pool store puts
+    codes and scales at the slot's page / row and skips negative slots."""
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((6, 2, 128)) * np.exp(rng.uniform(-8, 8, (6, 2, 1)))).astype(np.float32)
+    x[2, 1] = 0
+    codes, sc = O.quantize_rows_fp8(x)
+    amax = np.abs(x).max(-1)
+    assert np.array_equal(sc, (amax / np.float32(448)).astype(np.float32))
+    back = O.e4m3_decode(codes) * sc[..., None]
+    rel = np.abs(back - x) / np.maximum(amax[..., None], 1e-30)
+    assert rel.max() <= 16 / 448 * 1.001  # half the widest e4m3 step (32 in [256, 448]) of amax
+    assert sc[2, 1] == 0 and not codes[2, 1].any()
+    P, nb = 16, 2
+    kc = np.zeros((nb, P, 2, 128), np.uint8)
+    vc = kc.copy()
+    ks = np.full((nb, 2, P), -1, np.float32)
+    vs = ks.copy()
+    slots = np.array([17, -1, 3, 30, 0, 5])
+    O.store_kvcache_fp8(x, x, kc, vc, ks, vs, slots)
+    assert np.array_equal(kc[1, 1], codes[0]) and np.array_equal(ks[1, :, 1], sc[0])
+    assert np.array_equal(kc[0, 3], codes[2]) and (ks[0, :, 2] == -1).all()
