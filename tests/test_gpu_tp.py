@@ -17,8 +17,9 @@ NCCL.
 The greedy-stream gate of tests/test_gpu_greedy.py also runs at TP2: the
 config-1 model sharded over two GPUs against the CPU restatement of the
 reference (bf16 rounding points) built from the same weights, with the same
-two bars (teacher forced, and the GPU's free-running stream checked by the
-reference, each >= 95 % of positions).
+bars (test_gpu_greedy.passes: teacher forced, and the GPU's free-running
+stream checked by the reference, each >= 95 % of positions counting bf16
+near-ties; exact teacher-forced agreement >= 90 %).
 
 Skipped with fewer GPUs than ranks.  NVLS is off (NCCL_NVLS_ENABLE=0).
 """
@@ -79,22 +80,38 @@ def _worker(rank, world, port, route, q):
 
 
 def _greedy_tp(rank, world, dev):
-    """The config-1 greedy gate with the model at TP=world."""
+    """The config-1 greedy gate with the model at TP=world.  Rank 0 alone
+    runs the CPU reference and hands its stream to the other ranks over a
+    gloo group with a long timeout (the NCCL group's short one would expire
+    while rank 0 computes)."""
+    import datetime
+
     import torch.distributed as dist
 
     import nvkv
     import test_gpu_greedy as G
     from nvkv.decoder import Qwen3TP
-    full = Qwen3TP(G.CFG, 0, 1, seed=3, device=dev, **G.INIT)  # every rank: TP1 weights
-    w = G.to_numpy_weights(full)
-    del full
+    cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+
+    def share(obj):
+        box = [obj]
+        dist.broadcast_object_list(box, src=0, group=cpu)
+        return box[0]
+
+    w = None
+    if rank == 0:
+        full = Qwen3TP(G.CFG, 0, 1, seed=3, device=dev, **G.INIT)  # the TP1 weights
+        w = G.to_numpy_weights(full)
+        del full
     model = Qwen3TP(G.CFG, rank, world, seed=3, device=dev, **G.INIT)
-    report = G.gate(model, w)
+    report = G.gate(model, w, root=rank == 0, share=share)
     torch.cuda.synchronize()
     assert nvkv.device_error() == 0
-    dist.barrier()
+    ok = share(None if rank else G.passes(report))
+    dist.barrier(group=cpu)
     model.close()
-    ok = report["teacher_forced"] >= 0.95 and report["gpu_stream_checked_by_reference"] >= 0.95
+    if rank == 0:
+        print("TP%d greedy agreement" % world, report)
     return "ok" if ok else repr(report)
 
 
