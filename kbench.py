@@ -411,6 +411,8 @@ CASES = {
         "decode_cfg2", np.random.default_rng(2).integers(512, 4097, 64), 16, 8, 2048, it, 4),
     "decode_8b_tp1": lambda it: case_decode(
         "decode_8b_tp1", np.random.default_rng(4).integers(1025, 1537, 256), 32, 8, 1560, it, 2),
+    "decode_8b_tp2": lambda it: case_decode(
+        "decode_8b_tp2", np.random.default_rng(4).integers(1025, 1537, 256), 16, 4, 1560, it, 2),
     "decode_8b_tp8": lambda it: case_decode(
         "decode_8b_tp8", np.random.default_rng(4).integers(1025, 1537, 256), 4, 1, 1560, it, 8),
     "decode_8b_tp8_2k": lambda it: case_decode(
@@ -423,6 +425,9 @@ CASES = {
     "decode_8b_tp1_fp8": lambda it: case_decode_fp8(
         "decode_8b_tp1_fp8", np.random.default_rng(4).integers(1025, 1537, 256), 32, 8, 1560, it,
         2),
+    "decode_8b_tp2_fp8": lambda it: case_decode_fp8(
+        "decode_8b_tp2_fp8", np.random.default_rng(4).integers(1025, 1537, 256), 16, 4, 1560, it,
+        4),
     "decode_8b_tp8_fp8": lambda it: case_decode_fp8(
         "decode_8b_tp8_fp8", np.random.default_rng(4).integers(1025, 1537, 256), 4, 1, 1560, it,
         8),

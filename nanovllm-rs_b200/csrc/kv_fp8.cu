@@ -321,7 +321,7 @@ extern "C" int nvkv_paged_attention_fp8(
     return set_error(NVKV_ERR_UNSUPPORTED, "paged_attention_fp8: more than 2^31 cache rows");
   if (q_stride < (int64_t)num_q_heads * head_dim || (q_stride * 2) % 16 != 0 || !aligned16(q) ||
       !aligned16(out) || !aligned16(k_cache) || !aligned16(v_cache) ||
-      (reinterpret_cast<uintptr_t>(k_scale) & 3) || (reinterpret_cast<uintptr_t>(v_scale) & 3))
+      !aligned16(k_scale) || !aligned16(v_scale))
     return set_error(NVKV_ERR_ALIGNMENT, "paged_attention_fp8: misaligned buffer or stride");
   if (!(softmax_scale > 0.f))
     return set_error(NVKV_ERR_INVALID_ARG, "paged_attention_fp8: softmax_scale must be > 0");

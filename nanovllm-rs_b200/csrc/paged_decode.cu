@@ -53,66 +53,42 @@ struct DecodeParams {
 };
 
 // fp8 (e4m3) pool: the producer stages each tile's K and V codes (64 rows x
-// 128 B, one TMA box each) in a 2-stage fp8 ring; two converter warps turn
-// them into the dtype tiles (x * its row's scale, rounded once) of a
-// 2-stage ring in exactly the layout TMA gives the bf16 kernel, so the
-// compute warps run the same per-tile code.  HBM sees half the K/V bytes.
-constexpr int kDec8Stages = 2;
-constexpr int kDec8ConvWarps = 2;
-constexpr int kDec8Threads = (kDecComputeWarps + 1 + kDec8ConvWarps) * 32;
-constexpr int kDec8CodeTile = kDecTile * kDecD;        // 8 KB of codes: one K (or V) tile
-constexpr int kDec8CodeStage = 2 * kDec8CodeTile;       // K + V codes
-constexpr int kDec8OffCodes = kDec8Stages * kDecStageBytes;
-constexpr int kDec8OffRow = kDec8OffCodes + kDec8Stages * kDec8CodeStage;
-constexpr int kDec8OffBars = kDec8OffRow + kDec8Stages * 8;
-constexpr int kDec8SmemBytes =
-    kDec8OffBars + 4 * kDec8Stages * 8 + kDecComputeWarps * 2 * 16 * 4 + 1024;
-static_assert(2 * kDec8SmemBytes <= 228 * 1024, "fp8 decode: two CTAs per SM");
+// 128 B, one TMA box each, SWIZZLE_128B) and the tile's 64 K and 64 V row
+// scales (two 256-byte bulk copies from [page][kv head][row]) in a 4-stage
+// ring; the compute warps widen the codes in registers (dec8_tile), so HBM
+// and shared memory each see half the bf16 K/V bytes.
+#ifndef NVKV_DEC8_STAGES
+#define NVKV_DEC8_STAGES 4
+#endif
+#ifndef NVKV_DEC8_CTAS_PER_SM
+#define NVKV_DEC8_CTAS_PER_SM 3
+#endif
+constexpr int kDec8Stages = NVKV_DEC8_STAGES;
+constexpr int kDec8CtasPerSm = NVKV_DEC8_CTAS_PER_SM;
+constexpr int kDec8CodeTile = kDecTile * kDecD;   // 8 KB: one K (or V) code tile
+constexpr int kDec8ScaleBytes = kDecTile * 4;     // one tile's row scales
+constexpr int kDec8StageTx = 2 * kDec8CodeTile + 2 * kDec8ScaleBytes;
+constexpr int kDec8StageBytes = 17 * 1024;        // keeps every code tile 1024-byte aligned
+static_assert(kDec8StageTx <= kDec8StageBytes, "fp8 decode stage layout");
+constexpr int kDec8OffBars = kDec8Stages * kDec8StageBytes;
+constexpr int kDec8SmemBytes = kDec8OffBars + 2 * kDec8Stages * 8 + kDecComputeWarps * 2 * 16 * 4 + 1024;
+static_assert(kDec8Stages * kDec8StageBytes >= kDecComputeWarps * 16 * kDecD * 4,
+              "fp8 decode: the final combine reuses the stage memory");
+static_assert(kDec8CtasPerSm * (kDec8SmemBytes + 1024) <= 228 * 1024, "fp8 decode: CTAs per SM");
 
-// Four e4m3 codes (a 32-bit word, lowest byte first) -> four floats.
-__device__ __forceinline__ void e4m3x4_to_f32(uint32_t w, float* f) {
-  uint32_t lo, hi;
-  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
-      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
-      : "=r"(lo), "=r"(hi)
-      : "r"(w));
-  const float2 a = __half22float2(*reinterpret_cast<__half2*>(&lo));
-  const float2 b = __half22float2(*reinterpret_cast<__half2*>(&hi));
-  f[0] = a.x;
-  f[1] = a.y;
-  f[2] = b.x;
-  f[3] = b.y;
-}
-
-// Converts row r (0..63) of one fp8 code tile (128 B rows, SWIZZLE_128B) into
-// the two 64-element halves of the dtype tile at dst (SWIZZLE_128B), each
-// value times `scale`.
-template <typename T>
-__device__ __forceinline__ void dec8_convert_row(const uint8_t* codes, uint8_t* dst, int r,
-                                                 float scale) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds d = 16c .. 16c + 15
-    const uint4 w = *reinterpret_cast<const uint4*>(codes + r * 128 + ((c ^ (r & 7)) * 16));
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    uint32_t out[8];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float f[4];
-      e4m3x4_to_f32(ws[k], f);
-      out[2 * k] = DT<T>::from_f2(__fmul_rn(f[0], scale), __fmul_rn(f[1], scale));
-      out[2 * k + 1] = DT<T>::from_f2(__fmul_rn(f[2], scale), __fmul_rn(f[3], scale));
-    }
-    uint8_t* half = dst + (c >> 2) * kDecHalfBytes + r * 128;
-    const int j0 = (2 * c) & 7, j1 = (2 * c + 1) & 7;
-    *reinterpret_cast<uint4*>(half + ((j0 ^ (r & 7)) * 16)) =
-        make_uint4(out[0], out[1], out[2], out[3]);
-    *reinterpret_cast<uint4*>(half + ((j1 ^ (r & 7)) * 16)) =
-        make_uint4(out[4], out[5], out[6], out[7]);
-  }
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 template <typename T, bool kHi, bool kFp8>
-__global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
+__global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
   constexpr int kStages = kFp8 ? kDec8Stages : kDecStages;
@@ -121,10 +97,8 @@ __global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(
       smem + (kFp8 ? kDec8OffBars : kDecStages * kDecStageBytes));
   uint64_t* empty = full + kStages;
-  uint64_t* code_full = empty + kStages;        // fp8: the stage's codes landed
-  uint64_t* code_empty = code_full + kStages;   // fp8: the stage's codes converted
-  float* red = reinterpret_cast<float*>(kFp8 ? code_empty + kStages : empty + kStages);
-  int64_t* stage_row = reinterpret_cast<int64_t*>(smem + kDec8OffRow);  // fp8: first row
+  float* red = reinterpret_cast<float*>(empty + kStages);
+  constexpr int kStageStride = kFp8 ? kDec8StageBytes : kDecStageBytes;
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -132,12 +106,8 @@ __global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kFp8 ? kDec8ConvWarps : 1);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], kDecComputeWarps);
-      if (kFp8) {
-        mbar_init(&code_full[s], 1);
-        mbar_init(&code_empty[s], kDec8ConvWarps);
-      }
     }
     fence_mbar_init();
   }
@@ -177,40 +147,13 @@ __global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
   if (k_len <= 0 && threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
   __syncthreads();
 
-  if (kFp8 && warp > kDecComputeWarps) {
-    // ------------------------------ fp8 converters ------------------------------
-    const int r = (warp - kDecComputeWarps - 1) * 32 + lane;  // tile row 0..63
-    for (int it = 0; it < ntiles; ++it) {
-      const int s = it % kStages;
-      const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-      if (!mbar_wait(&code_full[s], ph, p.err)) break;
-      if (it >= kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
-      // the row's scales: [page][kv head][row in page]
-      const int64_t row = stage_row[s] + r;
-      const int64_t page = row / p.page_size;
-      const int64_t si = (page * p.num_kv_heads + kvh) * p.page_size + row % p.page_size;
-      const float ks = __ldg(p.k_scale + si), vs = __ldg(p.v_scale + si);
-      const uint8_t* codes = smem + kDec8OffCodes + s * kDec8CodeStage;
-      uint8_t* dst = smem + s * kDecStageBytes;
-      dec8_convert_row<T>(codes, dst, r, ks);
-      dec8_convert_row<T>(codes + kDec8CodeTile, dst + kDecTileBytes, r, vs);
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&code_empty[s]);
-        mbar_arrive(&full[s]);
-      }
-    }
-    return;
-  }
-
   if (warp == kDecComputeWarps) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       for (int it = 0; it < ntiles; ++it) {
         const int s = it % kStages;
         const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-        uint64_t* reuse = kFp8 ? &code_empty[s] : &empty[s];
-        if (it >= kStages && !mbar_wait(reuse, ph ^ 1u, p.err)) break;
+        if (it >= kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
         const int j0 = tok_begin + it * kDecTile;
         int64_t row;
         if (it == 0 && p.block_tables) {
@@ -225,11 +168,17 @@ __global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
                              j0, p.err);
         }
         if (kFp8) {
-          uint8_t* codes = smem + kDec8OffCodes + s * kDec8CodeStage;
-          stage_row[s] = row;  // published by the arrive below
-          mbar_arrive_expect_tx(&code_full[s], kDec8CodeStage);
-          tma_load_3d(codes, &tmap_k, &code_full[s], 0, kvh, (int)row);
-          tma_load_3d(codes + kDec8CodeTile, &tmap_v, &code_full[s], 0, kvh, (int)row);
+          // scales of the tile's rows: [page][kv head][row in page], 64
+          // consecutive floats (tiles never straddle a page)
+          uint8_t* st = smem + s * kDec8StageBytes;
+          const int64_t si =
+              ((row / p.page_size) * p.num_kv_heads + kvh) * p.page_size + row % p.page_size;
+          mbar_arrive_expect_tx(&full[s], kDec8StageTx);
+          tma_load_3d(st, &tmap_k, &full[s], 0, kvh, (int)row);
+          tma_load_3d(st + kDec8CodeTile, &tmap_v, &full[s], 0, kvh, (int)row);
+          bulk_load(st + 2 * kDec8CodeTile, p.k_scale + si, kDec8ScaleBytes, &full[s]);
+          bulk_load(st + 2 * kDec8CodeTile + kDec8ScaleBytes, p.v_scale + si, kDec8ScaleBytes,
+                    &full[s]);
         } else {
           dec_load_stage(smem + s * kDecStageBytes, &full[s], &tmap_k, &tmap_v, kvh, row);
         }
@@ -244,20 +193,31 @@ __global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
   const int r0 = lane >> 2, r1 = r0 + 8;
   const int cq = (lane & 3) * 2;
   uint32_t qa[8][4];
-  dec_load_q<T>(qa, reinterpret_cast<const T*>(p.q) + (int64_t)q0 * p.q_stride + (int64_t)hq0 * kDecD,
-                g, lane);
+  const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)q0 * p.q_stride + (int64_t)hq0 * kDecD;
+  if constexpr (kFp8)
+    dec8_load_q<T>(qa, qrow, g, lane);
+  else
+    dec_load_q<T>(qa, qrow, g, lane);
   DecState st;
   st.reset();
+  uint32_t vexp = 0;  // fp8: O is held in units of 2^(vexp - 127)
 
   for (int it = 0; it < ntiles; ++it) {
     const int s = it % kStages;
     const uint32_t ph = (uint32_t)(it / kStages) & 1u;
     if (!mbar_wait(&full[s], ph, p.err)) break;
-    const uint32_t kbase = smem_u32(smem + s * kDecStageBytes);
+    const uint32_t kbase = smem_u32(smem + s * kStageStride);
     const int valid = tok_end - (tok_begin + it * kDecTile + warp * 16);  // keys of this slice
-    if (valid > 0)
-      dec_tile<T, kHi>(qa, st, kbase, kbase + kDecTileBytes, warp * 16, valid, p.scale_log2,
-                       lane);
+    if (valid > 0) {
+      if constexpr (kFp8) {
+        const float* sc = reinterpret_cast<const float*>(smem + s * kStageStride + 2 * kDec8CodeTile);
+        dec8_tile<kHi>(qa, st, vexp, kbase, kbase + kDec8CodeTile, sc, sc + kDecTile, warp * 16,
+                       valid, p.scale_log2, lane);
+      } else {
+        dec_tile<T, kHi>(qa, st, kbase, kbase + kDecTileBytes, warp * 16, valid, p.scale_log2,
+                         lane);
+      }
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -284,14 +244,29 @@ __global__ void __launch_bounds__(kFp8 ? kDec8Threads : kDecThreads, 2)
       ms0 = fmaxf(ms0, red[(w * 2) * 16 + r0]);
       ms1 = fmaxf(ms1, red[(w * 2) * 16 + r1]);
     }
-    const float f0 = exp2f(st.m0 - (ms0 == -INFINITY ? 0.f : ms0));
-    const float f1 = exp2f(st.m1 - (ms1 == -INFINITY ? 0.f : ms1));
+    float f0 = exp2f(st.m0 - (ms0 == -INFINITY ? 0.f : ms0));
+    float f1 = exp2f(st.m1 - (ms1 == -INFINITY ? 0.f : ms1));
     float* ow = ofin + warp * 16 * kDecD;
+    if constexpr (kFp8) {
+      // O in units of 2^E; column n of d-tile dn is D = 16n + dn
+      f0 *= pow2_field(vexp);
+      f1 *= pow2_field(vexp);
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      const int d = n * 8 + cq;
-      *reinterpret_cast<float2*>(ow + r0 * kDecD + d) = make_float2(st.o[n][0] * f0, st.o[n][1] * f0);
-      *reinterpret_cast<float2*>(ow + r1 * kDecD + d) = make_float2(st.o[n][2] * f1, st.o[n][3] * f1);
+      for (int n = 0; n < 16; ++n) {
+        ow[r0 * kDecD + 16 * cq + n] = st.o[n][0] * f0;
+        ow[r0 * kDecD + 16 * (cq + 1) + n] = st.o[n][1] * f0;
+        ow[r1 * kDecD + 16 * cq + n] = st.o[n][2] * f1;
+        ow[r1 * kDecD + 16 * (cq + 1) + n] = st.o[n][3] * f1;
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        const int d = n * 8 + cq;
+        *reinterpret_cast<float2*>(ow + r0 * kDecD + d) =
+            make_float2(st.o[n][0] * f0, st.o[n][1] * f0);
+        *reinterpret_cast<float2*>(ow + r1 * kDecD + d) =
+            make_float2(st.o[n][2] * f1, st.o[n][3] * f1);
+      }
     }
   }
   named_bar_sync(1, kDecComputeWarps * 32);
@@ -410,7 +385,7 @@ static int launch_decode_grid(bool hi, dim3 grid, const CUtensorMap& mk, const C
                               const DecodeParams& p, cudaStream_t stream) {
   auto kern = hi ? paged_decode_kernel<T, true, kFp8> : paged_decode_kernel<T, false, kFp8>;
   constexpr int smem = kFp8 ? kDec8SmemBytes : kDecSmemBytes;
-  constexpr int threads = kFp8 ? kDec8Threads : kDecThreads;
+  constexpr int threads = kDecThreads;
   static unsigned long long attr_done[2] = {0, 0};  // per instantiation and kHi
   int rc = ensure_smem_attr((const void*)kern, smem, &attr_done[hi]);
   if (!rc)
