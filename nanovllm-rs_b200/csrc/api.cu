@@ -25,9 +25,9 @@ int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, int d) 
 }
 
 // Split-KV decode scratch, then (for max_seqlen_q > 1) the prefill work plan.
-size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k) {
+size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k, bool fp8) {
   if (num_seqs <= 0) return 0;
-  const size_t dec = decode_workspace_bytes(num_seqs, hq, hkv, max_k);
+  const size_t dec = decode_workspace_bytes(num_seqs, hq, hkv, max_k, fp8);
   const size_t plan = prefill_plan_bytes(num_seqs, max_q);
   return plan ? attention_plan_offset(dec) + plan : dec;
 }

@@ -94,15 +94,20 @@ struct AttnArgs {
   // page]; null for a bf16/f16 pool
   const float* k_scale = nullptr;
   const float* v_scale = nullptr;
+  // the workspace's split-KV scratch is sized for the fp8 decode plan (the
+  // prefill work plan follows it)
+  bool fp8_layout = false;
 };
 
 // Shared by the attention entry points (api.cu): shape checks, and the
 // workspace of split-KV scratch + prefill work plan.
 int validate_shapes(int num_seqs, int max_q, int max_k, int hq, int hkv, int d);
-size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k);
+size_t attention_workspace_bytes(int num_seqs, int hq, int hkv, int max_q, int max_k,
+                                 bool fp8 = false);
 int launch_paged_decode(const AttnArgs& a);
-size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k);
-void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
+size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k,
+                              bool fp8);
+void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, bool fp8, int* chunk_tokens,
                  int* max_splits);
 int launch_paged_prefill(const AttnArgs& a);
 // Bytes of the prefill work plan (0 when max_seqlen_q <= 1); it sits in the

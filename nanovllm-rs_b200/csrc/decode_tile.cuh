@@ -3,6 +3,8 @@
 // g = Hq/Hkv query heads of the kv group as the M = 16 rows of m16n8k16 MMAs.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace nvkv {
@@ -166,24 +168,28 @@ __device__ __forceinline__ void dec_tile(const uint32_t (&qa)[8][4], DecState& s
 }
 
 // ---------------------------------------------------------------------------
-// fp8 (e4m3) pool tiles.  The 64-row K and V code tiles (128 B rows,
-// SWIZZLE_128B) are read straight from shared memory with 16-byte loads and
-// widened in registers (cvt.rn.f16x2.e4m3x2: every e4m3 value is exact in
-// f16), so both products run as f16 m16n8k16 MMAs with f32 accumulation:
-//  * S = Q.codes^T: the reduction over D may visit D in any order as long as
-//    Q's A fragments follow the same order, so k-step kk of lane (g, t) takes
-//    D = 32t + 4kk + {0, 1} (b0) and + {2, 3} (b1): each lane reads 32
-//    contiguous code bytes of its key row.  S is then scaled per key column
-//    by that key's k-scale (fp32), which equals Q.(codes * k_scale) exactly.
-//  * O += P'.codes_V with P' = P * v_scale(key) * 2^-E: the output column
-//    order is free too (it is undone in the final combine), so d-tile dn,
-//    column n is D = 16n + dn: each lane reads 16 contiguous bytes of the four
-//    key rows of its B fragments and pairs them bytewise (prmt).  E is a
-//    running power of two >= the largest v-scale seen (its f32 exponent
-//    field), so P' stays in [0, 2) whatever the V magnitudes; O is kept in
-//    units of 2^E and rescaled (exactly) when E grows.
-// Q is converted to f16 once (exact for bf16 values within +-65504,
-// saturated beyond).
+// fp8 (e4m3) pool tiles, transposed products.  The K and V code tiles (64
+// rows of 128 B, SWIZZLE_128B) are read straight from shared memory with
+// 16-byte loads.  Keys and D take the M side of the MMAs and the query heads
+// of the group the N side (8 per n-tile, kNt = 1 for groups of <= 8 heads,
+// 2 for <= 16), so no M rows are padding:
+//  * S^T = codes_K . Q^T on m16n8k32 e4m3 MMAs.  A = the K code rows as they
+//    sit in shared memory: lane (g, t) reads 32 contiguous bytes of key rows
+//    g and g + 8 of its warp's 16 keys, and k-step kk covers D = 32t + 8kk +
+//    {0..3} (a0, a1) and + {4..7} (a2, a3) -- a reduction may visit D in any
+//    order as long as both operands follow it.  B = Q as a sum of e4m3 pieces
+//    (Dec8Q) in the same D order.  Each S^T row is then scaled by its key's
+//    k-scale, which equals Q.(codes * k_scale) exactly.
+//  * O^T += codes_V^T . P'^T on m16n8k16 f16 MMAs.  The order of O's D rows is
+//    free too (the final combine undoes it): m-tile mt, row m is D = 16(m mod
+//    8) + 8(m / 8) + mt, so lane (g, t) reads 16 contiguous bytes at D = 16g
+//    of key rows 2t, 2t + 1, 2t + 8, 2t + 9, pairs them bytewise (prmt) and
+//    widens them with cvt.rn.f16x2.e4m3x2 (every e4m3 value is exact in f16).
+//    P' = P * v_scale(key) * 2^-E, E a running power of two >= the largest
+//    v-scale seen (its f32 exponent field vexp), so P' < 2 whatever the V
+//    magnitudes; O is kept in units of 2^E and rescaled exactly when E grows.
+//    The S^T fragment holds P' per (key row, head pair); four shuffles per
+//    n-tile bring each lane the (key pair, head) entries of its B fragments.
 // ---------------------------------------------------------------------------
 
 // Four e4m3 codes (lowest byte first) -> two f16x2: codes {0,1} and {2,3}.
@@ -194,6 +200,13 @@ __device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_
       : "r"(w));
 }
 
+// e4m3 codes of (a, b), low byte = a (nearest even, saturating at 448)
+__device__ __forceinline__ uint32_t e4m3x2_pack(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
@@ -202,176 +215,343 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
-// two T values -> f16x2, saturated to the f16 range
-template <typename T>
-__device__ __forceinline__ uint32_t to_h2_sat(uint32_t u) {
-  const float2 f = DT<T>::to_f2(u);
-  return DT<__half>::from_f2(fminf(fmaxf(f.x, -65504.f), 65504.f),
-                             fminf(fmaxf(f.y, -65504.f), 65504.f));
-}
-
-// f16 A fragments of the g query rows in the D order above.
-template <typename T>
-__device__ __forceinline__ void dec8_load_q(uint32_t (&qa)[8][4], const T* qrow, int g, int lane) {
-  const int r0 = lane >> 2, r1 = r0 + 8, t = lane & 3;
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const int d = 32 * t + 4 * kk;
-    const uint2 x0 = r0 < g ? *reinterpret_cast<const uint2*>(qrow + r0 * kDecD + d) : make_uint2(0, 0);
-    const uint2 x1 = r1 < g ? *reinterpret_cast<const uint2*>(qrow + r1 * kDecD + d) : make_uint2(0, 0);
-    qa[kk][0] = to_h2_sat<T>(x0.x);
-    qa[kk][1] = to_h2_sat<T>(x1.x);
-    qa[kk][2] = to_h2_sat<T>(x0.y);
-    qa[kk][3] = to_h2_sat<T>(x1.y);
-  }
+// D = A.B + C, m16n8k32, A and B e4m3, f32 accumulate.
+__device__ __forceinline__ void mma_e4m3_16832(float (&c)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // 2^(e - 127) from an f32 exponent field e (0 -> 0.0)
 __device__ __forceinline__ float pow2_field(uint32_t e) { return __uint_as_float(e << 23); }
 
-// This warp's 16 keys [wtok, wtok + 16) of the fp8 tile: kbase / vbase are
-// the shared addresses of the K / V code tiles, ksc / vsc the tile's 64
-// per-row scales; vexp is the warp's running exponent field E + 127.
-template <bool kHi>
-__device__ __forceinline__ void dec8_tile(const uint32_t (&qa)[8][4], DecState& st, uint32_t& vexp,
+// Q as a sum of e4m3 pieces: Q * 2^sq = q_0 + q_1 (+ q_2), each piece the
+// e4m3 rounding of what the pieces before it left over.  sq puts the group's
+// largest |Q| just below 256, so two pieces hold a bf16 value exactly (8
+// significant bits: the first piece's rounding error is an integer multiple
+// of the value's ulp of at most 8 ulps) as long as |Q * 2^sq| >= 1/4, and
+// three pieces an f16 value; smaller elements keep at least 4 bits.
+template <typename T>
+struct Dec8Q {
+  static constexpr int kPieces = std::is_same<T, __half>::value ? 3 : 2;
+};
+
+// Lane (g, t) of n-tile j holds head 8j + g, D = 32t .. 32t + 31 of every
+// piece: qb[piece][j][w] = the codes of D = 32t + 4w .. 32t + 4w + 3.  Heads
+// >= g (the group size) are zero.  Returns 2^-sq.
+template <typename T, int kP, int kNt>
+__device__ __forceinline__ float dec8_load_q(uint32_t (&qb)[kP][kNt][8], const T* qrow, int g,
+                                             int lane) {
+  const int gq = lane >> 2, t = lane & 3;
+  float x[kNt][32];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNt; ++j) {
+    const int h = 8 * j + gq;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 u = h < g ? *reinterpret_cast<const uint4*>(qrow + h * kDecD + 32 * t + 8 * c)
+                            : make_uint4(0, 0, 0, 0);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = DT<T>::to_f2(w[k]);
+        x[j][8 * c + 2 * k] = f.x;
+        x[j][8 * c + 2 * k + 1] = f.y;
+        m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  // m * 2^sq < 256 <= 448 with sq = 7 - floor(log2 m)
+  const int e = (int)((__float_as_uint(m) >> 23) & 0xFFu);  // biased exponent of m
+  const int sq = m > 0.f ? min(127, 134 - e) : 0;
+  const float up = __uint_as_float((uint32_t)(127 + sq) << 23);
+#pragma unroll
+  for (int j = 0; j < kNt; ++j)
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[j][i] *= up;
+#pragma unroll
+  for (int pc = 0; pc < kP; ++pc) {
+#pragma unroll
+    for (int j = 0; j < kNt; ++j) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        float* v = &x[j][4 * w];
+        const uint32_t wd = e4m3x2_pack(v[0], v[1]) | (e4m3x2_pack(v[2], v[3]) << 16);
+        qb[pc][j][w] = wd;
+        if (pc + 1 < kP) {  // what this piece leaves over
+          uint32_t lo, hi;
+          e4m3x4_to_h2x2(wd, lo, hi);
+          const float2 a = DT<__half>::to_f2(lo), b = DT<__half>::to_f2(hi);
+          v[0] -= a.x;
+          v[1] -= a.y;
+          v[2] -= b.x;
+          v[3] -= b.y;
+        }
+      }
+    }
+  }
+  return __uint_as_float((uint32_t)(127 - sq) << 23);
+}
+
+// Online-softmax state of one warp, transposed: lane (g, t) holds, per n-tile
+// j, heads 8j + 2t + {0, 1}: their running max m (the same on every g), its
+// partial row sum l over the keys it saw, and O^T rows D = 16g + mt (o[..][0
+// / 1]) and 16g + 8 + mt (o[..][2 / 3]).
+template <int kNt>
+struct Dec8State {
+  float o[kNt][8][4];
+  float m[kNt][2], l[kNt][2];
+  uint32_t vexp;  // O in units of 2^(vexp - 127)
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int j = 0; j < kNt; ++j) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) o[j][n][0] = o[j][n][1] = o[j][n][2] = o[j][n][3] = 0.f;
+      m[j][0] = m[j][1] = -INFINITY;
+      l[j][0] = l[j][1] = 0.f;
+    }
+    vexp = 0;
+  }
+};
+
+__device__ __forceinline__ float dec_ex2(float x) {  // 2^x on MUFU (-inf -> 0)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// This warp's 32 keys [wtok, wtok + 32) of the fp8 tile, as two 16-key
+// halves u = 0, 1 (keys wtok + 16u + 0..15) that share one online-softmax
+// update: kbase / vbase are the shared addresses of the K / V code tiles,
+// ksc / vsc the tile's 64 row scales.  kPart: fewer than 32 of the keys
+// exist (`valid`), so the missing ones are masked (their codes may be stale
+// or NaN); otherwise nothing is.
+template <int kP, int kNt, bool kPart>
+__device__ __forceinline__ void dec8_tile(const uint32_t (&qb)[kP][kNt][8], Dec8State<kNt>& st,
                                           uint32_t kbase, uint32_t vbase, const float* ksc,
                                           const float* vsc, int wtok, int valid, float scale_log2,
                                           int lane) {
   const int t = lane & 3, gq = lane >> 2;
-  const int cq = 2 * t;
-  float sc[2][4];
+  // ---- S^T: key rows 16u + gq (x = 0) and 16u + gq + 8 (x = 1) ----
+  float s[2][kNt][4];  // [u][j][c]: c = 2x + e, head 8j + 2t + e
+  {
+    // rows r and r + 8k share r's swizzle phase: one offset per chunk
+    const uint32_t k0 = kbase + sw128_offset((uint32_t)(wtok + gq), 2 * t);
+    const uint32_t k1 = kbase + sw128_offset((uint32_t)(wtok + gq), 2 * t + 1);
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-    const uint32_t krow = (uint32_t)(wtok + nt * 8 + gq);
-    const uint4 w0 = lds128(kbase + sw128_offset(krow, 2 * t));
-    const uint4 w1 = lds128(kbase + sw128_offset(krow, 2 * t + 1));
-    const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    for (int u = 0; u < 2; ++u) {
+      const uint4 a0 = lds128(k0 + u * 2048), a1 = lds128(k1 + u * 2048);
+      const uint4 b0 = lds128(k0 + u * 2048 + 1024), b1 = lds128(k1 + u * 2048 + 1024);
+      const uint32_t ka[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const uint32_t kb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float acc[kNt][kP][4];  // one chain per (n-tile, piece): four MMAs deep
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t b0, b1;
-      e4m3x4_to_h2x2(w[kk], b0, b1);
-      mma_16816<__half>(sc[nt], qa[kk], b0, b1);
+      for (int j = 0; j < kNt; ++j)
+#pragma unroll
+        for (int pc = 0; pc < kP; ++pc) {
+          acc[j][pc][0] = acc[j][pc][1] = acc[j][pc][2] = acc[j][pc][3] = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_e4m3_16832(acc[j][pc], ka[2 * kk], kb[2 * kk], ka[2 * kk + 1], kb[2 * kk + 1],
+                           qb[pc][j][2 * kk], qb[pc][j][2 * kk + 1]);
+        }
+#pragma unroll
+      for (int j = 0; j < kNt; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v = acc[j][0][c];
+#pragma unroll
+          for (int pc = 1; pc < kP; ++pc) v += acc[j][pc][c];
+          s[u][j][c] = v;
+        }
     }
   }
-  float vs[2][2];
-  float mx0 = -INFINITY, mx1 = -INFINITY, vm = 0.f;
+  // the lane's four keys 16u + 8x + gq: scales, presence
+  float f[2][2], w[2][2];
+  bool ok[2][2];
+  float vm = 0.f;
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    const float2 ks = *reinterpret_cast<const float2*>(ksc + wtok + nt * 8 + cq);
-    const float2 v2 = *reinterpret_cast<const float2*>(vsc + wtok + nt * 8 + cq);
+  for (int u = 0; u < 2; ++u)
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const bool ok = (nt * 8 + cq + e) < valid;
-      const float f = (e ? ks.y : ks.x) * scale_log2;
-      vs[nt][e] = ok ? (e ? v2.y : v2.x) : 0.f;
-      vm = fmaxf(vm, vs[nt][e]);
-      sc[nt][e] = ok ? sc[nt][e] * f : -INFINITY;
-      mx0 = fmaxf(mx0, sc[nt][e]);
-      if (kHi) {
-        sc[nt][e + 2] = ok ? sc[nt][e + 2] * f : -INFINITY;
-        mx1 = fmaxf(mx1, sc[nt][e + 2]);
-      }
+    for (int x = 0; x < 2; ++x) {
+      const int k = 16 * u + 8 * x + gq;
+      ok[u][x] = !kPart || k < valid;
+      f[u][x] = ksc[wtok + k] * scale_log2;
+      w[u][x] = ok[u][x] ? vsc[wtok + k] : 0.f;
+      vm = fmaxf(vm, w[u][x]);
     }
-  }
-  // the 16 keys' largest v-scale (lanes of a quad hold all of them)
-  vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, 1));
-  vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, 2));
-  const uint32_t vnew = max(vexp, min(254u, __float_as_uint(vm) >> 23));  // inf/NaN: clamp
-  const float vfac = vnew == vexp ? 1.f
-                     : (int)(vnew - vexp) < 127 ? pow2_field(127u - (vnew - vexp)) : 0.f;
-  vexp = vnew;
+  // the 32 keys' largest v-scale
+  vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, 4));
+  vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, 8));
+  vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, 16));
+  const uint32_t vnew = max(st.vexp, min(254u, __float_as_uint(vm) >> 23));  // inf/NaN: clamp
+  const float vfac = vnew == st.vexp ? 1.f
+                     : (int)(vnew - st.vexp) < 127 ? pow2_field(127u - (vnew - st.vexp)) : 0.f;
+  st.vexp = vnew;
   const float vinv = pow2_field(254u - vnew);  // 2^-E
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int x = 0; x < 2; ++x) w[u][x] *= vinv;
 
-  mx0 = warp_max_xor(warp_max_xor(mx0, 1), 2);
-  const float mn0 = fmaxf(st.m0, mx0);
-  const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
-  const float al0 = exp2f(st.m0 - mu0);
-  st.m0 = mn0;
-  float al1 = 1.f;
-  if (kHi) {
-    mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
-    const float mn1 = fmaxf(st.m1, mx1);
-    const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-    al1 = exp2f(st.m1 - mu1);
-    st.m1 = mn1;
+  uint32_t xp[2][2][kNt];  // P' of key 16u + 8x + gq, heads 8j + 2t + {0, 1}
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      sc[nt][2] = exp2f(sc[nt][2] - mu1);
-      sc[nt][3] = exp2f(sc[nt][3] - mu1);
-    }
-    st.l1 = st.l1 * al1 + (sc[0][2] + sc[0][3] + sc[1][2] + sc[1][3]);
-  }
-  float ps0 = 0.f;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
+  for (int j = 0; j < kNt; ++j) {
+    float fac[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      sc[nt][e] = exp2f(sc[nt][e] - mu0);
-      ps0 += sc[nt][e];
-    }
-  }
-  st.l0 = st.l0 * al0 + ps0;
-  const float f0 = al0 * vfac, f1 = al1 * vfac;
-  if (f0 != 1.f || f1 != 1.f) {
+      float sv[2][2];
+      float mx = -INFINITY;
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      st.o[n][0] *= f0;
-      st.o[n][1] *= f0;
-      if (kHi) {
-        st.o[n][2] *= f1;
-        st.o[n][3] *= f1;
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          sv[u][x] = ok[u][x] ? s[u][j][2 * x + e] * f[u][x] : -INFINITY;
+          mx = fmaxf(mx, sv[u][x]);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(st.m[j][e], mx);
+      const float mu = mn == -INFINITY ? 0.f : mn;
+      const float al = dec_ex2(st.m[j][e] - mu);
+      st.m[j][e] = mn;
+      float ps = 0.f;
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float pv = dec_ex2(sv[u][x] - mu);
+          ps += pv;
+          s[u][j][2 * x + e] = pv * w[u][x];
+        }
+      st.l[j][e] = st.l[j][e] * al + ps;
+      fac[e] = al * vfac;
+    }
+    if (fac[0] != 1.f || fac[1] != 1.f) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        st.o[j][n][0] *= fac[0];
+        st.o[j][n][1] *= fac[1];
+        st.o[j][n][2] *= fac[0];
+        st.o[j][n][3] *= fac[1];
       }
     }
-  }
-  uint32_t pa[4];
-  const float w00 = vs[0][0] * vinv, w01 = vs[0][1] * vinv;
-  const float w10 = vs[1][0] * vinv, w11 = vs[1][1] * vinv;
-  pa[0] = DT<__half>::from_f2(sc[0][0] * w00, sc[0][1] * w01);
-  pa[1] = kHi ? DT<__half>::from_f2(sc[0][2] * w00, sc[0][3] * w01) : 0u;
-  pa[2] = DT<__half>::from_f2(sc[1][0] * w10, sc[1][1] * w11);
-  pa[3] = kHi ? DT<__half>::from_f2(sc[1][2] * w10, sc[1][3] * w11) : 0u;
-  // B fragment keys of this lane: wtok + cq + {0,1} (b0), + 8 + {0,1} (b1);
-  // missing keys' codes (stale rows, possibly NaN codes) are zeroed
-  const uint32_t keep_lo = (cq < valid ? 0x0000ffffu : 0u) | (cq + 1 < valid ? 0xffff0000u : 0u);
-  const uint32_t keep_hi =
-      (cq + 8 < valid ? 0x0000ffffu : 0u) | (cq + 9 < valid ? 0xffff0000u : 0u);
-  const uint32_t ra = (uint32_t)(wtok + cq), rb = ra + 8;
-  const uint4 A0 = lds128(vbase + sw128_offset(ra, gq));
-  const uint4 A1 = lds128(vbase + sw128_offset(ra + 1, gq));
-  const uint4 B0 = lds128(vbase + sw128_offset(rb, gq));
-  const uint4 B1 = lds128(vbase + sw128_offset(rb + 1, gq));
-  const uint32_t a0[4] = {A0.x, A0.y, A0.z, A0.w}, a1[4] = {A1.x, A1.y, A1.z, A1.w};
-  const uint32_t c0[4] = {B0.x, B0.y, B0.z, B0.w}, c1[4] = {B1.x, B1.y, B1.z, B1.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {  // bytes 4i .. 4i + 3 of each row: d-tiles dn = 4i .. 4i + 3
-    uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
-    e4m3x4_to_h2x2(__byte_perm(a0[i], a1[i], 0x5140), l0, l1);
-    e4m3x4_to_h2x2(__byte_perm(a0[i], a1[i], 0x7362), l2, l3);
-    e4m3x4_to_h2x2(__byte_perm(c0[i], c1[i], 0x5140), h0, h1);
-    e4m3x4_to_h2x2(__byte_perm(c0[i], c1[i], 0x7362), h2, h3);
-    mma_16816<__half>(st.o[4 * i + 0], pa, l0 & keep_lo, h0 & keep_hi);
-    mma_16816<__half>(st.o[4 * i + 1], pa, l1 & keep_lo, h1 & keep_hi);
-    mma_16816<__half>(st.o[4 * i + 2], pa, l2 & keep_lo, h2 & keep_hi);
-    mma_16816<__half>(st.o[4 * i + 3], pa, l3 & keep_lo, h3 & keep_hi);
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int x = 0; x < 2; ++x)
+        xp[u][x][j] = DT<__half>::from_f2(s[u][j][2 * x], s[u][j][2 * x + 1]);
+  }
+  // ---- O^T += V^T . P'^T, per half ----
+  // B fragments of n-tile j: b0 = P'[keys 2t, 2t + 1][head 8j + gq], b1 = the
+  // same for keys 2t + 8, 2t + 9 (of the half).  Key k's pair of heads
+  // (gq & ~1, gq | 1) sits in lane 4 (k mod 8) + gq / 2, in xp[u][k / 8].
+  const int src0 = 4 * (2 * t) + (gq >> 1), src1 = src0 + 4;
+  const uint32_t sel = (gq & 1) ? 0x7632u : 0x5410u;
+  const int cq = 2 * t;
+  const uint32_t v0 = vbase + sw128_offset((uint32_t)(wtok + cq), gq);
+  const uint32_t v1 = vbase + sw128_offset((uint32_t)(wtok + cq + 1), gq);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    uint32_t pb0[kNt], pb1[kNt];
+#pragma unroll
+    for (int j = 0; j < kNt; ++j) {
+      const uint32_t a0 = __shfl_sync(0xffffffffu, xp[u][0][j], src0);
+      const uint32_t a1 = __shfl_sync(0xffffffffu, xp[u][0][j], src1);
+      const uint32_t b0 = __shfl_sync(0xffffffffu, xp[u][1][j], src0);
+      const uint32_t b1 = __shfl_sync(0xffffffffu, xp[u][1][j], src1);
+      pb0[j] = __byte_perm(a0, a1, sel);
+      pb1[j] = __byte_perm(b0, b1, sel);
+    }
+    const int vk = valid - 16 * u;  // keys of this half that exist
+    const uint32_t keep_lo =
+        !kPart ? ~0u : (cq < vk ? 0x0000ffffu : 0u) | (cq + 1 < vk ? 0xffff0000u : 0u);
+    const uint32_t keep_hi =
+        !kPart ? ~0u : (cq + 8 < vk ? 0x0000ffffu : 0u) | (cq + 9 < vk ? 0xffff0000u : 0u);
+    // rows 16u + cq (+1) and + 8: the same swizzle phase as rows cq (+1)
+    const uint4 A0 = lds128(v0 + u * 2048), A1 = lds128(v1 + u * 2048);
+    const uint4 B0 = lds128(v0 + u * 2048 + 1024), B1 = lds128(v1 + u * 2048 + 1024);
+    const uint32_t x0[4] = {A0.x, A0.y, A0.z, A0.w}, x1[4] = {A1.x, A1.y, A1.z, A1.w};
+    const uint32_t y0[4] = {B0.x, B0.y, B0.z, B0.w}, y1[4] = {B1.x, B1.y, B1.z, B1.w};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {  // bytes 4i .. 4i + 3 (rows m < 8) and 8 + 4i .. (m >= 8)
+      uint32_t a[4][4];            // [mt - 4i][a0..a3]
+      e4m3x4_to_h2x2(__byte_perm(x0[i], x1[i], 0x5140), a[0][0], a[1][0]);
+      e4m3x4_to_h2x2(__byte_perm(x0[i], x1[i], 0x7362), a[2][0], a[3][0]);
+      e4m3x4_to_h2x2(__byte_perm(x0[i + 2], x1[i + 2], 0x5140), a[0][1], a[1][1]);
+      e4m3x4_to_h2x2(__byte_perm(x0[i + 2], x1[i + 2], 0x7362), a[2][1], a[3][1]);
+      e4m3x4_to_h2x2(__byte_perm(y0[i], y1[i], 0x5140), a[0][2], a[1][2]);
+      e4m3x4_to_h2x2(__byte_perm(y0[i], y1[i], 0x7362), a[2][2], a[3][2]);
+      e4m3x4_to_h2x2(__byte_perm(y0[i + 2], y1[i + 2], 0x5140), a[0][3], a[1][3]);
+      e4m3x4_to_h2x2(__byte_perm(y0[i + 2], y1[i + 2], 0x7362), a[2][3], a[3][3]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t af[4] = {a[q][0] & keep_lo, a[q][1] & keep_lo, a[q][2] & keep_hi,
+                                a[q][3] & keep_hi};
+#pragma unroll
+        for (int j = 0; j < kNt; ++j) mma_16816<__half>(st.o[j][4 * i + q], af, pb0[j], pb1[j]);
+      }
+    }
   }
 }
 
-// TMA row of key tile j0 of sequence b: through the page table (pages of
-// page_size rows; an out-of-range page id is recorded and read as page 0 so
-// the waiting consumers still get their bytes) or contiguous from cu_k[b].
-__device__ __forceinline__ int64_t dec_tile_row(const uint32_t* block_tables, int64_t bt_stride,
-                                                int64_t num_blocks, int page_size,
-                                                const uint32_t* cu_k, int b, int j0, int* err) {
-  if (block_tables) {
-    uint32_t page = block_tables[(int64_t)b * bt_stride + j0 / page_size];
-    if ((int64_t)page >= num_blocks) {
-      record_error(err, NVKV_DEVERR_BLOCK_RANGE);
-      page = 0;
+// Column of D = d of head h in the fp8 path's final-combine buffer: the low
+// five bits are XOR-ed with (d / 32 mod 4, h / 2 mod 4), so a warp's scatter
+// of its O^T fragments and the row-wise reads both hit 32 distinct banks.
+__device__ __forceinline__ int dec8_ofin_col(int d, int h) {
+  return (d & ~31) | ((d & 31) ^ (((d >> 5) & 3) | (((h >> 1) & 3) << 2)));
+}
+
+// The warp's (m, l) per head into red ([warp][m | l][16]) and its O rows,
+// times `f`(head) * 2^E, into ow ([16 heads][128], dec8_ofin_col order).
+template <int kNt>
+__device__ __forceinline__ void dec8_put_ml(Dec8State<kNt>& st, float* red, int warp, int lane) {
+  const int t = lane & 3, gq = lane >> 2;
+#pragma unroll
+  for (int j = 0; j < kNt; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float l = st.l[j][e];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      st.l[j][e] = l;
+      if (gq == 0) {
+        const int h = 8 * j + 2 * t + e;
+        red[(warp * 2 + 0) * 16 + h] = st.m[j][e];
+        red[(warp * 2 + 1) * 16 + h] = l;
+      }
     }
-    return (int64_t)page * page_size + (j0 % page_size);
-  }
-  return (int64_t)cu_k[b] + j0;
+}
+
+template <int kNt>
+__device__ __forceinline__ void dec8_put_o(const Dec8State<kNt>& st, const float* red,
+                                           float* ow, int nwarps, int lane) {
+  const int t = lane & 3, gq = lane >> 2;
+  const float p2 = pow2_field(st.vexp);
+#pragma unroll
+  for (int j = 0; j < kNt; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int h = 8 * j + 2 * t + e;
+      float ms = -INFINITY;
+      for (int w = 0; w < nwarps; ++w) ms = fmaxf(ms, red[(w * 2) * 16 + h]);
+      const float f = exp2f(st.m[j][e] - (ms == -INFINITY ? 0.f : ms)) * p2;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int d0 = 16 * gq + n, d1 = d0 + 8;
+        ow[h * kDecD + dec8_ofin_col(d0, h)] = st.o[j][n][e] * f;
+        ow[h * kDecD + dec8_ofin_col(d1, h)] = st.o[j][n][e + 2] * f;
+      }
+    }
 }
 
 // Four TMA loads of one stage: K and V, the two 64-element halves of D.

@@ -212,7 +212,7 @@ struct F8Layout {
 };
 F8Layout f8_layout(int num_seqs, int hq, int hkv, int max_q, int max_k, int64_t prompt_rows) {
   F8Layout L;
-  L.base = attention_workspace_bytes(num_seqs, hq, hkv, max_q, max_k);
+  L.base = attention_workspace_bytes(num_seqs, hq, hkv, max_q, max_k, true);
   if (max_q <= 1 || num_seqs <= 0) {
     L.cu_kd = L.kbuf = L.vbuf = L.total = L.base;
     return L;
@@ -358,6 +358,7 @@ extern "C" int nvkv_paged_attention_fp8(
   a.stream = reinterpret_cast<cudaStream_t>(stream);
   a.k_scale = k_scale;
   a.v_scale = v_scale;
+  a.fp8_layout = true;
   if (max_seqlen_q > 1 && prompt_kv_tokens == 0)
     return set_error(NVKV_ERR_INVALID_ARG,
                      "paged_attention_fp8: max_seqlen_q > 1 needs prompt_kv_tokens >= the "

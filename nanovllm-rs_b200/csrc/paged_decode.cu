@@ -20,6 +20,8 @@
 //
 // Roofline: HBM.  Algorithmic bytes per (sequence, kv head) = 2*L*D*2 (K, V)
 // plus q/out rows; nothing is re-read across query heads.
+#include <algorithm>
+
 #include "decode_tile.cuh"
 
 namespace nvkv {
@@ -39,7 +41,7 @@ struct DecodeParams {
   int num_q_heads;
   int group;
   int page_size;
-  int chunk_tokens;  // keys per split, multiple of kDecTile
+  int chunk_tokens;  // keys per split, a multiple of the kernel's tile
   int max_k;         // max_seqlen_k: the block tables cover this many keys
   int64_t num_q_rows;  // rows of q and out
   int max_splits;
@@ -52,26 +54,35 @@ struct DecodeParams {
   int num_kv_heads;
 };
 
-// fp8 (e4m3) pool: the producer stages each tile's K and V codes (64 rows x
-// 128 B, one TMA box each, SWIZZLE_128B) and the tile's 64 K and 64 V row
-// scales (two 256-byte bulk copies from [page][kv head][row]) in a 4-stage
-// ring; the compute warps widen the codes in registers (dec8_tile), so HBM
-// and shared memory each see half the bf16 K/V bytes.
+// fp8 (e4m3) pool: 128-key tiles.  The producer stages each tile's K and V
+// codes (128 rows x 128 B, one TMA box each, SWIZZLE_128B) and the tile's
+// 128 K and 128 V row scales (two 512-byte bulk copies from [page][kv head]
+// [row]) in a 3-stage ring, two CTAs per SM; each compute warp runs the transposed e4m3 / f16
+// products of dec8_tile on 32 keys of every tile, on the codes in place, so
+// HBM and shared memory each see half the bf16 K/V bytes.  A tile carries as
+// many bytes as a 64-key bf16 tile: the per-tile costs of the copy pipeline
+// (measured to bound 64-key fp8 tiles well below the HBM peak) stay the
+// same per byte.
+// Measured (8B decode at TP1/2/8, 32B at TP8): 3 stages x 2 CTAs per SM
+// beat 2 x 3 everywhere (equal at TP1, 20.6 against 31.2 us at TP8, where
+// 256 CTAs fill one wave and each CTA's bytes in flight set its pace).
 #ifndef NVKV_DEC8_STAGES
-#define NVKV_DEC8_STAGES 4
+#define NVKV_DEC8_STAGES 3
 #endif
 #ifndef NVKV_DEC8_CTAS_PER_SM
-#define NVKV_DEC8_CTAS_PER_SM 3
+#define NVKV_DEC8_CTAS_PER_SM 2
 #endif
+constexpr int kDec8Tile = 128;
 constexpr int kDec8Stages = NVKV_DEC8_STAGES;
 constexpr int kDec8CtasPerSm = NVKV_DEC8_CTAS_PER_SM;
-constexpr int kDec8CodeTile = kDecTile * kDecD;   // 8 KB: one K (or V) code tile
-constexpr int kDec8ScaleBytes = kDecTile * 4;     // one tile's row scales
+constexpr int kDec8CodeTile = kDec8Tile * kDecD;   // 16 KB: one K (or V) code tile
+constexpr int kDec8ScaleBytes = kDec8Tile * 4;     // one tile's row scales
 constexpr int kDec8StageTx = 2 * kDec8CodeTile + 2 * kDec8ScaleBytes;
-constexpr int kDec8StageBytes = 17 * 1024;        // keeps every code tile 1024-byte aligned
+constexpr int kDec8StageBytes = 34 * 1024;         // keeps every code tile 1024-byte aligned
 static_assert(kDec8StageTx <= kDec8StageBytes, "fp8 decode stage layout");
 constexpr int kDec8OffBars = kDec8Stages * kDec8StageBytes;
-constexpr int kDec8SmemBytes = kDec8OffBars + 2 * kDec8Stages * 8 + kDecComputeWarps * 2 * 16 * 4 + 1024;
+constexpr int kDec8SmemBytes =
+    kDec8OffBars + 2 * kDec8Stages * 8 + kDecComputeWarps * 2 * 16 * 4 + 1024;
 static_assert(kDec8Stages * kDec8StageBytes >= kDecComputeWarps * 16 * kDecD * 4,
               "fp8 decode: the final combine reuses the stage memory");
 static_assert(kDec8CtasPerSm * (kDec8SmemBytes + 1024) <= 228 * 1024, "fp8 decode: CTAs per SM");
@@ -92,13 +103,13 @@ __global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
   constexpr int kStages = kFp8 ? kDec8Stages : kDecStages;
+  constexpr int kTile = kFp8 ? kDec8Tile : kDecTile;  // keys per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(
       smem + (kFp8 ? kDec8OffBars : kDecStages * kDecStageBytes));
   uint64_t* empty = full + kStages;
   float* red = reinterpret_cast<float*>(empty + kStages);
-  constexpr int kStageStride = kFp8 ? kDec8StageBytes : kDecStageBytes;
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -120,15 +131,17 @@ __global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
   pdl_launch_dependents();
   pdl_wait();  // inputs may come from the previous kernel in the stream
 
-  // The producer fetches the page of its first tile together with the
-  // sequence lengths (one round trip less before the first TMA).  The index
-  // depends only on the split, and split * chunk_tokens < the plan's key
-  // bound <= page_size * bt_stride (validated on the host), so it is in
-  // bounds even for a split this sequence does not have.
-  uint32_t first_page = 0;
-  if (threadIdx.x == kDecComputeWarps * 32 && p.block_tables)
-    first_page = __ldg(p.block_tables + (int64_t)b * p.bt_stride +
-                       (split * p.chunk_tokens) / p.page_size);
+  // The producer warp reads its chunk's block-table entries 32 pages at a
+  // time, one coalesced load, the first of them together with the sequence
+  // lengths (one round trip less before the first TMA), and hands lane 0 each
+  // tile's page by a shuffle, so no tile waits on a dependent global load.
+  // The first chunk page depends only on the split, and split * chunk_tokens
+  // < the plan's key bound <= page_size * bt_stride (validated on the host),
+  // so every entry read below lies inside this sequence's table row.
+  const int pg_first = (split * p.chunk_tokens) / p.page_size;
+  uint32_t ent = 0;
+  if (warp == kDecComputeWarps && p.block_tables && pg_first + lane < p.bt_stride)
+    ent = __ldg(p.block_tables + (int64_t)b * p.bt_stride + pg_first + lane);
 
   const uint32_t q0 = p.cu_q[b];
   if (p.cu_q[b + 1] - q0 != 1) return;  // not a decode row: the prefill kernel owns it
@@ -143,32 +156,40 @@ __global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
   }
   const int tok_begin = split * p.chunk_tokens;
   const int tok_end = min(k_len, tok_begin + p.chunk_tokens);
-  const int ntiles = tok_end > tok_begin ? (tok_end - tok_begin + kDecTile - 1) / kDecTile : 0;
+  const int ntiles = tok_end > tok_begin ? (tok_end - tok_begin + kTile - 1) / kTile : 0;
   if (k_len <= 0 && threadIdx.x == 0) record_error(p.err, NVKV_DEVERR_SEQLEN);
   __syncthreads();
 
   if (warp == kDecComputeWarps) {
     // ------------------------------ TMA producer ------------------------------
-    if (lane == 0) {
-      for (int it = 0; it < ntiles; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-        if (it >= kStages && !mbar_wait(&empty[s], ph ^ 1u, p.err)) break;
-        const int j0 = tok_begin + it * kDecTile;
-        int64_t row;
-        if (it == 0 && p.block_tables) {
-          uint32_t page = first_page;
-          if ((int64_t)page >= p.num_blocks) {
-            record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
-            page = 0;
-          }
-          row = (int64_t)page * p.page_size + (j0 % p.page_size);
-        } else {
-          row = dec_tile_row(p.block_tables, p.bt_stride, p.num_blocks, p.page_size, p.cu_k, b,
-                             j0, p.err);
+    const int64_t row0 = p.block_tables ? 0 : (int64_t)p.cu_k[b];  // contiguous rows
+    int ent_base = 0;  // chunk page held by lane 0's entry
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % kStages;
+      const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+      const int j0 = tok_begin + it * kTile;
+      int64_t row;
+      if (p.block_tables) {
+        const int pi = j0 / p.page_size - pg_first;  // page within the chunk
+        if (pi >= ent_base + 32) {  // warp-uniform: the next 32 entries
+          ent_base += 32;
+          const int pg = pg_first + ent_base + lane;
+          ent = pg < p.bt_stride ? __ldg(p.block_tables + (int64_t)b * p.bt_stride + pg) : 0u;
         }
-        if (kFp8) {
-          // scales of the tile's rows: [page][kv head][row in page], 64
+        uint32_t page = __shfl_sync(0xffffffffu, ent, pi - ent_base);
+        if ((int64_t)page >= p.num_blocks) {  // recorded; read as page 0 so the consumers finish
+          if (lane == 0) record_error(p.err, NVKV_DEVERR_BLOCK_RANGE);
+          page = 0;
+        }
+        row = (int64_t)page * p.page_size + (j0 % p.page_size);
+      } else {
+        row = row0 + j0;
+      }
+      int go = 1;
+      if (lane == 0) {
+        go = it < kStages || mbar_wait(&empty[s], ph ^ 1u, p.err);
+        if (go && kFp8) {
+          // scales of the tile's rows: [page][kv head][row in page], 128
           // consecutive floats (tiles never straddle a page)
           uint8_t* st = smem + s * kDec8StageBytes;
           const int64_t si =
@@ -179,10 +200,11 @@ __global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
           bulk_load(st + 2 * kDec8CodeTile, p.k_scale + si, kDec8ScaleBytes, &full[s]);
           bulk_load(st + 2 * kDec8CodeTile + kDec8ScaleBytes, p.v_scale + si, kDec8ScaleBytes,
                     &full[s]);
-        } else {
+        } else if (go) {
           dec_load_stage(smem + s * kDecStageBytes, &full[s], &tmap_k, &tmap_v, kvh, row);
         }
       }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
     }
     return;
   }
@@ -190,83 +212,83 @@ __global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
   // ------------------------------ compute warps ------------------------------
   const int g = p.group;
   const int hq0 = kvh * g;
-  const int r0 = lane >> 2, r1 = r0 + 8;
-  const int cq = (lane & 3) * 2;
-  uint32_t qa[8][4];
   const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)q0 * p.q_stride + (int64_t)hq0 * kDecD;
-  if constexpr (kFp8)
-    dec8_load_q<T>(qa, qrow, g, lane);
-  else
+  float* ofin = reinterpret_cast<float*>(smem);  // [warp][16][128] fp32 = 32 KB, after the loop
+  if constexpr (kFp8) {
+    constexpr int kP = Dec8Q<T>::kPieces, kNt = kHi ? 2 : 1;
+    uint32_t qb[kP][kNt][8];
+    const float s_log2 = p.scale_log2 * dec8_load_q<T, kP, kNt>(qb, qrow, g, lane);
+    Dec8State<kNt> st;
+    st.reset();
+    const int wtok = warp * 32;  // this warp's keys of every tile
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % kStages;
+      const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+      if (!mbar_wait(&full[s], ph, p.err)) break;
+      uint8_t* stage = smem + s * kDec8StageBytes;
+      const uint32_t kbase = smem_u32(stage);
+      const float* sc = reinterpret_cast<const float*>(stage + 2 * kDec8CodeTile);
+      const int valid = tok_end - (tok_begin + it * kDec8Tile + wtok);  // this warp's keys
+      if (valid >= 32)
+        dec8_tile<kP, kNt, false>(qb, st, kbase, kbase + kDec8CodeTile, sc, sc + kDec8Tile, wtok,
+                                  valid, s_log2, lane);
+      else if (valid > 0)
+        dec8_tile<kP, kNt, true>(qb, st, kbase, kbase + kDec8CodeTile, sc, sc + kDec8Tile, wtok,
+                                 valid, s_log2, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    dec8_put_ml<kNt>(st, red, warp, lane);
+    named_bar_sync(1, kDecComputeWarps * 32);  // all loops done: stage memory is free
+    dec8_put_o<kNt>(st, red, ofin + warp * 16 * kDecD, kDecComputeWarps, lane);
+  } else {
+    const int r0 = lane >> 2, r1 = r0 + 8;
+    const int cq = (lane & 3) * 2;
+    uint32_t qa[8][4];
     dec_load_q<T>(qa, qrow, g, lane);
-  DecState st;
-  st.reset();
-  uint32_t vexp = 0;  // fp8: O is held in units of 2^(vexp - 127)
-
-  for (int it = 0; it < ntiles; ++it) {
-    const int s = it % kStages;
-    const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-    if (!mbar_wait(&full[s], ph, p.err)) break;
-    const uint32_t kbase = smem_u32(smem + s * kStageStride);
-    const int valid = tok_end - (tok_begin + it * kDecTile + warp * 16);  // keys of this slice
-    if (valid > 0) {
-      if constexpr (kFp8) {
-        const float* sc = reinterpret_cast<const float*>(smem + s * kStageStride + 2 * kDec8CodeTile);
-        dec8_tile<kHi>(qa, st, vexp, kbase, kbase + kDec8CodeTile, sc, sc + kDecTile, warp * 16,
-                       valid, p.scale_log2, lane);
-      } else {
+    DecState st;
+    st.reset();
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it % kStages;
+      const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+      if (!mbar_wait(&full[s], ph, p.err)) break;
+      const uint32_t kbase = smem_u32(smem + s * kDecStageBytes);
+      const int valid = tok_end - (tok_begin + it * kDecTile + warp * 16);  // keys of this slice
+      if (valid > 0)
         dec_tile<T, kHi>(qa, st, kbase, kbase + kDecTileBytes, warp * 16, valid, p.scale_log2,
                          lane);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
 
-  // ------------------------------ warp combine ------------------------------
-  float l0 = st.l0, l1 = st.l1;
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  if ((lane & 3) == 0) {
-    red[(warp * 2 + 0) * 16 + r0] = st.m0;
-    red[(warp * 2 + 1) * 16 + r0] = l0;
-    red[(warp * 2 + 0) * 16 + r1] = st.m1;
-    red[(warp * 2 + 1) * 16 + r1] = l1;
-  }
-  named_bar_sync(1, kDecComputeWarps * 32);  // all loops done: stage memory is free
+    // ------------------------------ warp combine ------------------------------
+    float l0 = st.l0, l1 = st.l1;
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if ((lane & 3) == 0) {
+      red[(warp * 2 + 0) * 16 + r0] = st.m0;
+      red[(warp * 2 + 1) * 16 + r0] = l0;
+      red[(warp * 2 + 0) * 16 + r1] = st.m1;
+      red[(warp * 2 + 1) * 16 + r1] = l1;
+    }
+    named_bar_sync(1, kDecComputeWarps * 32);  // all loops done: stage memory is free
 
-  float* ofin = reinterpret_cast<float*>(smem);  // [warp][16][128] fp32 = 32 KB
-  {
     float ms0 = -INFINITY, ms1 = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kDecComputeWarps; ++w) {
       ms0 = fmaxf(ms0, red[(w * 2) * 16 + r0]);
       ms1 = fmaxf(ms1, red[(w * 2) * 16 + r1]);
     }
-    float f0 = exp2f(st.m0 - (ms0 == -INFINITY ? 0.f : ms0));
-    float f1 = exp2f(st.m1 - (ms1 == -INFINITY ? 0.f : ms1));
+    const float f0 = exp2f(st.m0 - (ms0 == -INFINITY ? 0.f : ms0));
+    const float f1 = exp2f(st.m1 - (ms1 == -INFINITY ? 0.f : ms1));
     float* ow = ofin + warp * 16 * kDecD;
-    if constexpr (kFp8) {
-      // O in units of 2^E; column n of d-tile dn is D = 16n + dn
-      f0 *= pow2_field(vexp);
-      f1 *= pow2_field(vexp);
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        ow[r0 * kDecD + 16 * cq + n] = st.o[n][0] * f0;
-        ow[r0 * kDecD + 16 * (cq + 1) + n] = st.o[n][1] * f0;
-        ow[r1 * kDecD + 16 * cq + n] = st.o[n][2] * f1;
-        ow[r1 * kDecD + 16 * (cq + 1) + n] = st.o[n][3] * f1;
-      }
-    } else {
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const int d = n * 8 + cq;
-        *reinterpret_cast<float2*>(ow + r0 * kDecD + d) =
-            make_float2(st.o[n][0] * f0, st.o[n][1] * f0);
-        *reinterpret_cast<float2*>(ow + r1 * kDecD + d) =
-            make_float2(st.o[n][2] * f1, st.o[n][3] * f1);
-      }
+    for (int n = 0; n < 16; ++n) {
+      const int d = n * 8 + cq;
+      *reinterpret_cast<float2*>(ow + r0 * kDecD + d) = make_float2(st.o[n][0] * f0, st.o[n][1] * f0);
+      *reinterpret_cast<float2*>(ow + r1 * kDecD + d) = make_float2(st.o[n][2] * f1, st.o[n][3] * f1);
     }
   }
   named_bar_sync(1, kDecComputeWarps * 32);
@@ -281,7 +303,7 @@ __global__ void __launch_bounds__(kDecThreads, kFp8 ? kDec8CtasPerSm : 2)
 #pragma unroll
     for (int w = 0; w < kDecComputeWarps; ++w) {
       ls += red[(w * 2 + 1) * 16 + r] * exp2f(red[(w * 2) * 16 + r] - mu);
-      acc += ofin[(w * 16 + r) * kDecD + tid];
+      acc += ofin[(w * 16 + r) * kDecD + (kFp8 ? dec8_ofin_col(tid, r) : tid)];
     }
     const float val = ls > 0.f ? acc / ls : 0.f;
     const int hq = hq0 + r;
@@ -330,18 +352,20 @@ __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParam
 // Host side
 // ---------------------------------------------------------------------------
 
-// Split-KV plan: enough CTAs for ~3 resident waves at 2 CTAs/SM, but never
-// chunks shorter than 12 tiles (768 keys): a sweep over the decode shapes of
-// configs 2, 4 (TP1, TP8) and 5 found this the best or equal-best everywhere
-// (shorter chunks pay per-CTA setup and merge work on small per-GPU batches).
-// Exception: when one CTA per (sequence, kv head) already fills >= 80 % of a
-// resident wave and no sequence exceeds NVKV_DECODE_ONE_WAVE_MAX_TILES tiles,
-// nothing is split -- a single wave with no combine beats 1.7 waves plus a
-// combine (8B TP8, 256 seqs: 37.2 -> 31.1 us at ctx <= 1536, 54.7 -> 45.6 us
-// at ctx <= 2560).  The cost is bounded by the tile cap: one long sequence
-// among short ones then runs unsplit (+1.3 us measured at 24 tiles).
-#ifndef NVKV_DECODE_TARGET_CTAS
-#define NVKV_DECODE_TARGET_CTAS (148 * 2 * 3)
+// Split-KV plan: enough CTAs for ~3 resident waves (a wave = 148 SMs x the
+// kernel's CTAs per SM: 2 for bf16/f16 pools, kDec8CtasPerSm for fp8), but
+// never chunks shorter than 12 tiles (768 keys): a sweep over the decode
+// shapes of configs 2, 4 (TP1, TP8) and 5 found this the best or equal-best
+// everywhere (shorter chunks pay per-CTA setup and merge work on small
+// per-GPU batches).  Exception: when one CTA per (sequence, kv head) already
+// fills >= 80 % of a resident wave and no sequence exceeds
+// NVKV_DECODE_ONE_WAVE_MAX_TILES tiles, nothing is split -- a single wave
+// with no combine beats 1.7 waves plus a combine (8B TP8, 256 seqs: 37.2 ->
+// 31.1 us at ctx <= 1536, 54.7 -> 45.6 us at ctx <= 2560).  The cost is
+// bounded by the tile cap: one long sequence among short ones then runs
+// unsplit (+1.3 us measured at 24 tiles).
+#ifndef NVKV_DECODE_WAVES
+#define NVKV_DECODE_WAVES 3
 #endif
 #ifndef NVKV_DECODE_MIN_TILES
 #define NVKV_DECODE_MIN_TILES 12
@@ -349,25 +373,31 @@ __global__ void __launch_bounds__(kDecD) decode_combine_kernel(const DecodeParam
 #ifndef NVKV_DECODE_ONE_WAVE_MAX_TILES
 #define NVKV_DECODE_ONE_WAVE_MAX_TILES 48
 #endif
-void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, int* chunk_tokens,
+void decode_plan(int num_seqs, int num_kv_heads, int max_seqlen_k, bool fp8, int* chunk_tokens,
                  int* max_splits) {
-  const int tiles = max_seqlen_k > 0 ? (max_seqlen_k + kDecTile - 1) / kDecTile : 1;
+  const int ctas_per_sm = fp8 ? kDec8CtasPerSm : 2;
+  const int tile = fp8 ? kDec8Tile : kDecTile;
+  const int tiles = max_seqlen_k > 0 ? (max_seqlen_k + tile - 1) / tile : 1;
   const int64_t items = (int64_t)num_seqs * num_kv_heads;
-  const int64_t target = NVKV_DECODE_TARGET_CTAS;
-  const int64_t wave = 148 * 2;
+  const int64_t wave = 148 * (int64_t)ctas_per_sm;
+  const int64_t target = NVKV_DECODE_WAVES * wave;
   int splits = (int)((target + items - 1) / items);
-  const int max_by_len = (tiles + NVKV_DECODE_MIN_TILES - 1) / NVKV_DECODE_MIN_TILES;
+  // the limits are stated in 64-key units
+  const int min_tiles = std::max(1, NVKV_DECODE_MIN_TILES * kDecTile / tile);
+  const int max_by_len = (tiles + min_tiles - 1) / min_tiles;
   if (splits > max_by_len) splits = max_by_len;
-  if (items * 5 >= wave * 4 && tiles <= NVKV_DECODE_ONE_WAVE_MAX_TILES) splits = 1;
+  if (items * 5 >= wave * 4 && tiles * tile <= NVKV_DECODE_ONE_WAVE_MAX_TILES * kDecTile)
+    splits = 1;
   if (splits < 1) splits = 1;
   const int tiles_per_split = (tiles + splits - 1) / splits;
-  *chunk_tokens = tiles_per_split * kDecTile;
+  *chunk_tokens = tiles_per_split * tile;
   *max_splits = (tiles + tiles_per_split - 1) / tiles_per_split;
 }
 
-size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k) {
+size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int max_seqlen_k,
+                              bool fp8) {
   int chunk, splits;
-  decode_plan(num_seqs, num_kv_heads, max_seqlen_k, &chunk, &splits);
+  decode_plan(num_seqs, num_kv_heads, max_seqlen_k, fp8, &chunk, &splits);
   if (splits <= 1) return 0;
   const size_t n = (size_t)num_seqs * splits * num_q_heads;
   return n * kDecD * sizeof(float) + n * sizeof(float) + 256;
@@ -394,16 +424,16 @@ static int launch_decode_grid(bool hi, dim3 grid, const CUtensorMap& mk, const C
 }
 
 int launch_paged_decode(const AttnArgs& a) {
-  int chunk, splits;
-  decode_plan(a.num_seqs, a.hkv, a.max_k, &chunk, &splits);
-  const int64_t rows = a.block_tables ? a.num_blocks * a.page : a.num_blocks;
   const bool fp8 = a.k_scale != nullptr;
+  int chunk, splits;
+  decode_plan(a.num_seqs, a.hkv, a.max_k, fp8, &chunk, &splits);
+  const int64_t rows = a.block_tables ? a.num_blocks * a.page : a.num_blocks;
   CUtensorMap mk, mv;
   int rc;
   if (fp8) {  // paged only; rows of Hkv x 128 one-byte codes
-    rc = encode_kv_tensor_map_u8(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride, kDecTile);
+    rc = encode_kv_tensor_map_u8(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride, kDec8Tile);
     if (!rc)
-      rc = encode_kv_tensor_map_u8(&mv, a.v_cache, kDecD, a.hkv, rows, a.kv_stride, kDecTile);
+      rc = encode_kv_tensor_map_u8(&mv, a.v_cache, kDecD, a.hkv, rows, a.kv_stride, kDec8Tile);
   } else {
     rc = encode_kv_tensor_map(&mk, a.k_cache, kDecD, a.hkv, rows, a.kv_stride * 2, 64, kDecTile,
                               true);

@@ -894,7 +894,7 @@ int launch_paged_prefill(const AttnArgs& a) {
     return set_error(NVKV_ERR_UNSUPPORTED, "paged prefill: too many tiles");
   if (items == 0) return NVKV_OK;
   const size_t plan_off =
-      attention_plan_offset(decode_workspace_bytes(a.num_seqs, a.hq, a.hkv, a.max_k));
+      attention_plan_offset(decode_workspace_bytes(a.num_seqs, a.hq, a.hkv, a.max_k, a.fp8_layout));
   const size_t plan_need = prefill_plan_bytes(a.num_seqs, a.max_q);
   if (!a.ws || a.ws_bytes < plan_off + plan_need)
     return set_error(NVKV_ERR_WORKSPACE, "paged prefill: workspace too small for the work plan");
