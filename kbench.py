@@ -73,6 +73,11 @@ def _time(fn, iters, warmup=3):
     return a.elapsed_time(b) * 1e-3 / iters, None
 
 
+# --copies N: every paged-decode case keeps only N copies of its pool (a small
+# case for an ncu capture; timings then run on L2-warm inputs when N is small)
+COPIES = None
+
+
 def _paged(lens, page, hkv, nblocks, seed, copies=1):
     g = torch.Generator(device="cuda").manual_seed(seed)
     rng = np.random.default_rng(seed)
@@ -127,6 +132,7 @@ def case_prologue(T, iters):
 
 
 def case_decode(name, lens, hq, hkv, nblocks, iters, copies=1):
+    copies = COPIES or copies
     page = 256
     caches, bt = _paged(lens, page, hkv, nblocks, 3, copies)
     B = len(lens)
@@ -150,6 +156,7 @@ def case_decode_fp8(name, lens, hq, hkv, nblocks, iters, copies=1):
     """case_decode over the fp8 (e4m3) pool: codes and per-row scales written
     by nvkv_store_kvcache_fp8 from random rows.  Algorithmic bytes: one byte
     per K/V value plus the 4-byte row scales, q and out, block tables."""
+    copies = COPIES or copies
     page = 256
     caches, bt = _paged(lens, page, hkv, nblocks, 3, copies)
     pools = []
@@ -446,7 +453,11 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", nargs="*", default=list(CASES))
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--copies", type=int, default=None,
+                    help="pool copies per paged-decode case (default: the case's own)")
     a = ap.parse_args(argv)
+    global COPIES
+    COPIES = a.copies
     hbm, tf, src = _peaks()
     for name in a.case:
         r = CASES[name](a.iters)

@@ -5,10 +5,13 @@ nvkv_rms_norm on the same inputs.
 One GPU: a world-1 communicator (the sum is the input itself), which must
 give nvkv_rms_norm's bits exactly, eagerly and under CUDA-graph replay.
 Two or more GPUs (skipped otherwise): one spawned process per GPU.  At
-world 2 the sum of two bf16 values rounded once is what NCCL computes too,
-so results must be bit-identical; at larger worlds NCCL's ring rounds at
-every hop, so the tolerance is one bf16 ulp of the sum propagated through the
-norm (max-abs 2e-2).  A timeout case lets one rank skip the call: the other
+every world size the result must equal, bit for bit, the exact reference:
+all partials gathered, summed in fp32 in rank order, rounded once, then
+nvkv_rms_norm (bench.allreduce_reference).  Against NCCL: at world 2 the sum
+of two bf16 values rounded once is what NCCL computes too, so results must be
+bit-identical; at larger worlds NCCL's ring rounds at every hop, so the
+residual sum may differ by up to world bf16 ulps of sum |partials| +
+|residual|.  A timeout case lets one rank skip the call: the other
 rank's bounded waits must expire into NVKV_DEVERR_PEER_TIMEOUT with its
 context still usable.
 """
@@ -113,6 +116,9 @@ def _worker(rank, world, port, mode, q):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=60))
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import bench
         from nvkv.comm import PeerComm
         comm = PeerComm(rank, world, 1024 * 5120 * 2, timeout_s=0.2 if mode == "timeout" else None)
         if mode == "timeout":
@@ -138,16 +144,20 @@ def _worker(rank, world, port, mode, q):
                 comm.input(T, H).copy_(part)
                 res, out = r.clone(), torch.empty(T, H, dtype=torch.bfloat16, device=dev)
                 comm.allreduce_rms_norm(T, H, res, w, 1e-6, out)
+                parts = [torch.empty_like(part) for _ in range(world)]
+                dist.all_gather(parts, part)
                 ref = part.clone()
                 dist.all_reduce(ref)
                 res_ref = r.clone()
                 out_ref = ops.rms_norm(ref, w, 1e-6, residual=res_ref) if T else ref
                 torch.cuda.synchronize()
+                if T:
+                    res_e, out_e, bound = bench.allreduce_reference(parts, r, w, 1e-6, world)
+                    assert torch.equal(res, res_e) and torch.equal(out, out_e), (T, H)
                 if world == 2:
                     assert torch.equal(res, res_ref) and torch.equal(out, out_ref), (T, H)
                 elif T:
-                    assert (res.float() - res_ref.float()).abs().max() <= 2e-2 * 4, (T, H)
-                    assert (out.float() - out_ref.float()).abs().max() <= 2e-2 * 4, (T, H)
+                    assert ((res.float() - res_ref.float()).abs() <= bound).all(), (T, H)
             # graph replays keep the device epochs of all ranks in lockstep
             T, H = 256, 4096
             part = torch.randn(T, H, generator=torch.Generator().manual_seed(rank)).to(
@@ -214,6 +224,11 @@ def test_two_ranks_match_nccl_bitwise():
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
 def test_four_ranks_match_nccl():
     _run(4, "parity")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 8, reason="needs 8 GPUs")
+def test_eight_ranks_match_nccl():
+    _run(8, "parity")
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")

@@ -8,9 +8,11 @@ their all-reduces, vocab-parallel embedding and lm_head) and the same slice
 unsharded, runs four prompts through one prefill step and greedy decode
 steps fed with the TP=1 tokens, and requires:
   * the TP=N greedy token equal to TP=1's at >= 95 % of positions;
-  * the fused all-reduce + residual + RMSNorm bit-identical to NCCL's
-    all-reduce + nvkv_rms_norm at TP2 (within one bf16 ulp of the sum at
-    TP4).
+  * the fused all-reduce + residual + RMSNorm bit-identical to the exact
+    reference (partials summed in fp32 in rank order, rounded once, then
+    nvkv_rms_norm) at every TP, and to NCCL's all-reduce + nvkv_rms_norm at
+    TP2 (within world bf16 ulps of sum |partials| + |residual| at TP4, where
+    NCCL's ring rounds at every hop).
 Both all-reduce routes of the model are run: the nvkv peer-memory kernel and
 NCCL.
 
