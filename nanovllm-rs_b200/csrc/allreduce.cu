@@ -36,7 +36,9 @@
 // locally.
 //
 // Small messages (at most kArLLMaxBytes, e.g. a decode step's 256 x 4096
-// rows) take the low-latency (LL) form of the same two protocols instead:
+// rows) between two ranks take the low-latency (LL) form of the one-shot
+// protocol instead (a two-shot LL form measured slower than the flag
+// hand-off at 8 ranks, 33.5 against 24.4 us per 2 MiB call, and was removed):
 // every 8-byte word pushed to a peer carries 4 bytes of data and the call's
 // epoch in its upper half, stored and polled as single-copy-atomic 64-bit
 // words (st/ld.relaxed.sys).  The receiver spins on the words themselves, so
@@ -44,7 +46,7 @@
 // the hand-off: a hand-off costs the data's flight time, at twice the bytes.
 // Large messages keep the flag hand-off, whose fixed cost is small next to
 // their transfer.  Both forms sum in the same order and give the same bits.
-//   LL buffers: recv_ll [2 parities][world][ll_region], gath_ll [2][ll_region]
+//   LL buffers: recv_ll [2 parities][world][ll_region]
 //   (ll_region = 2 x the data bytes of kArLLMaxBytes).
 //
 // Every wait is bounded by the communicator's timeout (%globaltimer); on
@@ -66,7 +68,7 @@ struct ArParams {
   int64_t region;              // bytes of one [max_tokens, hidden] buffer slot
   int64_t off_recv, off_gath, off_flag;
   int64_t ll_region;           // bytes of one LL [rows, hidden] slot (2 x the data)
-  int64_t off_recv_ll, off_gath_ll;
+  int64_t off_recv_ll;
   uint32_t* epoch;             // this rank's per-CTA epochs
   int rank, world;
   int two_shot;
@@ -128,9 +130,6 @@ __device__ __forceinline__ uint8_t* ar_recv_ll(const ArParams& p, int q, int par
                                                int64_t row) {
   return p.base[q] + p.off_recv_ll + ((int64_t)par * p.world + src) * p.ll_region +
          row * p.H * 4;
-}
-__device__ __forceinline__ uint8_t* ar_gath_ll(const ArParams& p, int q, int par, int64_t row) {
-  return p.base[q] + p.off_gath_ll + (int64_t)par * p.ll_region + row * p.H * 4;
 }
 // Pushes vector v (16 data bytes) as 4 LL words of epoch e at dst (32 bytes).
 __device__ __forceinline__ void st_ll(uint8_t* dst, uint4 v, uint32_t e) {
@@ -336,7 +335,8 @@ __device__ __forceinline__ uint4 sum_vals(const uint4* v, int W) {
   return o;
 }
 
-// The LL form of the kernel above (same rows per CTA, same sums, same norm).
+// The LL form of the kernel's one-shot protocol (same rows per CTA, same
+// sums, same norm).
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) allreduce_rms_norm_ll_kernel(const ArParams p) {
   __shared__ float red[kNormThreads / 32];
@@ -361,63 +361,28 @@ __global__ void __launch_bounds__(kNormThreads) allreduce_rms_norm_ll_kernel(con
     return __ldcg(reinterpret_cast<const uint4*>(in + u * rb + (int64_t)c * 16));
   };
 
-  if (!p.two_shot) {
-    // ---- one-shot: push every row of this CTA to every peer, sum on arrival ----
-    for (int64_t u = b; u < p.T; u += kArCtas)
-      for (int c = tid; c < nvec; c += kNormThreads) {
-        const uint4 v = mine(u, c);
+  // ---- one-shot: push every row of this CTA to every peer, sum on arrival ----
+  for (int64_t u = b; u < p.T; u += kArCtas)
+    for (int c = tid; c < nvec; c += kNormThreads) {
+      const uint4 v = mine(u, c);
 #pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
-          if (q < W && q != r) st_ll(ar_recv_ll(p, q, par, r, u) + (int64_t)c * 32, v, e);
-      }
-    for (int64_t u = b; u < p.T; u += kArCtas) {
-      T* ru = res + u * H;
-      norm_row_load<T>(
-          [&](int c) {
-            uint4 v[kArMaxRanks];
+      for (int q = 0; q < kArMaxRanks; ++q)
+        if (q < W && q != r) st_ll(ar_recv_ll(p, q, par, r, u) + (int64_t)c * 32, v, e);
+    }
+  for (int64_t u = b; u < p.T; u += kArCtas) {
+    T* ru = res + u * H;
+    norm_row_load<T>(
+        [&](int c) {
+          uint4 v[kArMaxRanks];
 #pragma unroll
-            for (int q = 0; q < kArMaxRanks; ++q)
-              if (q < W)
-                v[q] = q == r ? mine(u, c)
-                              : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
-                                      p.timeout_ns, fail, p.err);
-            return sum_vals<T>(v, W);
-          },
-          p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
-    }
-  } else {
-    // ---- two-shot: push each row to its owner; owners sum and push to all ----
-    for (int64_t u = b; u < p.T; u += kArCtas) {
-      const int o = (int)(u / p.S);
-      if (o == r) continue;
-      for (int c = tid; c < nvec; c += kNormThreads)
-        st_ll(ar_recv_ll(p, o, par, r, u) + (int64_t)c * 32, mine(u, c), e);
-    }
-    for (int64_t u = b; u < p.T; u += kArCtas) {
-      if ((int)(u / p.S) != r) continue;
-      for (int c = tid; c < nvec; c += kNormThreads) {
-        uint4 v[kArMaxRanks];
-#pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
-          if (q < W)
-            v[q] = q == r ? mine(u, c)
-                          : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
-                                  p.timeout_ns, fail, p.err);
-        const uint4 s = sum_vals<T>(v, W);
-#pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
-          if (q < W) st_ll(ar_gath_ll(p, q, par, u) + (int64_t)c * 32, s, e);
-      }
-    }
-    for (int64_t u = b; u < p.T; u += kArCtas) {
-      T* ru = res + u * H;
-      norm_row_load<T>(
-          [&](int c) {
-            return ld_ll(ar_gath_ll(p, r, par, u) + (int64_t)c * 32, e, p.timeout_ns, fail,
-                         p.err);
-          },
-          p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
-    }
+          for (int q = 0; q < kArMaxRanks; ++q)
+            if (q < W)
+              v[q] = q == r ? mine(u, c)
+                            : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
+                                    p.timeout_ns, fail, p.err);
+          return sum_vals<T>(v, W);
+        },
+        p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
   }
   __syncthreads();
   if (tid == 0 && !s_fail) p.epoch[b] = e;
@@ -452,10 +417,9 @@ size_t epoch_off(const nvkv_comm* c) { return flag_off(c) + round256(kFlagBytes)
 // LL slots hold 2 bytes of word per data byte, for messages up to kArLLMaxBytes
 size_t ll_region(const nvkv_comm* c) { return 2 * std::min(c->region, kArLLMaxBytes); }
 size_t recv_ll_off(const nvkv_comm* c) { return epoch_off(c) + round256(kEpochBytes); }
-size_t gath_ll_off(const nvkv_comm* c) {
+size_t total_bytes(const nvkv_comm* c) {
   return recv_ll_off(c) + 2 * (size_t)c->world * ll_region(c);
 }
-size_t total_bytes(const nvkv_comm* c) { return gath_ll_off(c) + 2 * ll_region(c); }
 
 // One-shot (every rank pushes its whole partial to every peer, one barrier)
 // for two ranks; two-shot (push to the row's owner, owner reduces and
@@ -601,7 +565,6 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   p.off_flag = (int64_t)flag_off(c);
   p.ll_region = (int64_t)ll_region(c);
   p.off_recv_ll = (int64_t)recv_ll_off(c);
-  p.off_gath_ll = (int64_t)gath_ll_off(c);
   p.epoch = reinterpret_cast<uint32_t*>(c->base + epoch_off(c));
   p.rank = c->rank;
   p.world = c->world;
@@ -618,8 +581,11 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   p.timeout_ns = c->timeout_ns;
   p.err = device_error_word();
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // every rank sees the same num_tokens, so every rank takes the same form
-  const bool ll = (size_t)num_tokens * (size_t)hidden * 2 <= kArLLMaxBytes;
+  // every rank sees the same num_tokens, so every rank takes the same form.
+  // LL only for the one-shot protocol: its words double the bytes pushed,
+  // which two-shot at 8 ranks paid for (33.5 us per 2 MiB call against 24.4
+  // with the flag hand-off), while two ranks gain (15.8 us, NCCL 28.2).
+  const bool ll = !p.two_shot && (size_t)num_tokens * (size_t)hidden * 2 <= kArLLMaxBytes;
   if (dtype == NVKV_DTYPE_BF16) {
     if (ll)
       allreduce_rms_norm_ll_kernel<__nv_bfloat16><<<kArCtas, kNormThreads, 0, s>>>(p);
