@@ -46,6 +46,7 @@ typedef struct CUstream_st* nvkv_stream_t; /* == cudaStream_t */
 
 #define NVKV_DTYPE_F16 0
 #define NVKV_DTYPE_BF16 1
+#define NVKV_DTYPE_F32 2 /* logits of nvkv_sample only */
 
 /* Device-side error codes reported by nvkv_device_error(). */
 #define NVKV_DEVERR_NONE 0
@@ -269,6 +270,29 @@ int nvkv_rms_norm(const void* x, int64_t x_stride, void* residual, int64_t resid
 
 int nvkv_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
                       int64_t num_tokens, int inter, int dtype, nvkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * On-device sampling.  Replaces Sampler::forward
+ * (nanovllm_rs/src/layers/sampler.rs:7-21: softmax(logits / T) / E,
+ * E = max(-log U, 1e-10), argmax) by its Gumbel-max equivalent
+ *   token = argmax_v  logit[v] / T - log(max(-log u_v, 1e-10))
+ * which needs no softmax pass: the log-sum-exp the softmax subtracts is the
+ * same for every v of a row.  u_v comes from Philox4x32-10 keyed by `seed`,
+ * counter (global index / 4, row, step low 32 bits, step high 32 bits),
+ * u = ((bits >> 9) + 1/2) 2^-23, so the noise of an element depends only on
+ * (seed, step, row, global vocab index): a vocab-parallel shard
+ * (vocab_offset = the global index of its column 0) gives the same
+ * candidates as the whole vocabulary, and the largest value over the shards
+ * (ties to the lowest index) is the whole row's sample.  Temperatures <= 0
+ * give the plain arg-max (greedy).
+ * logits: [num_rows, row_stride] of dtype NVKV_DTYPE_BF16 / F16 / F32 (the
+ * first `vocab` columns are read); temperatures [num_rows] f32; out_value
+ * [num_rows] f32 (the winning score), out_index [num_rows] i64 (its global
+ * vocab index).  All device memory.
+ * ---------------------------------------------------------------------- */
+int nvkv_sample(const void* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
+                int64_t vocab_offset, const float* temperatures, uint64_t seed, uint64_t step,
+                float* out_value, int64_t* out_index, int dtype, nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Device-side metadata of a pure decode step.  Replaces the decode case of

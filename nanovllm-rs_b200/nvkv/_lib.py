@@ -23,6 +23,7 @@ ERR_DEVICE = -6
 
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
+DTYPE_F32 = 2  # nvkv_sample's logits only
 
 DEVERR_NONE = 0
 DEVERR_SLOT_RANGE = 1
@@ -89,6 +90,8 @@ SIGNATURES = {
     "nvkv_rms_norm": [_p, _i64, _p, _i64, _p, _f32, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_silu_and_mul": [_p, _i64, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_decode_advance": [_i32, _i32, _p, _p, _i64, _i64, _p, _p, _p, _p, _p],
+    "nvkv_sample": [_p, _i64, _i64, _i64, _i64, _p, ctypes.c_uint64, ctypes.c_uint64, _p, _p,
+                    _i32, _p],
     "nvkv_comm_create": [_i32, _i32, _sz, ctypes.POINTER(_p), _p],
     "nvkv_comm_open_peers": [_p, _p],
     "nvkv_comm_input": [_p, ctypes.POINTER(_p)],

@@ -103,7 +103,12 @@ def vocab_parallel_argmax(local: torch.Tensor, rank: int, group=None) -> torch.T
     index -- exactly argmax over the concatenated logits (gather_logits) at
     T x 16 bytes per rank instead of T x V/tp x 4."""
     v, i = local.max(dim=-1)
-    gi = i + rank * local.size(-1)
+    return vocab_parallel_pick(v, i + rank * local.size(-1), group)
+
+
+def vocab_parallel_pick(v: torch.Tensor, gi: torch.Tensor, group=None) -> torch.Tensor:
+    """The row-wise winner over the ranks' (value, global index) candidates:
+    the largest value, ties to the lowest index."""
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return gi
     ws = dist.get_world_size(group)
@@ -317,6 +322,16 @@ class Qwen3TP:
         if self.tp == 1:
             return local.argmax(dim=-1)
         return vocab_parallel_argmax(local, self.rank, self.group)
+
+    def sample(self, st: Step, temperatures: torch.Tensor, seed: int, step: int) -> torch.Tensor:
+        """The sampled next token of every sequence, [B] int64: the
+        reference's Sampler::forward (layers/sampler.rs:7-21) over forward()'s
+        logits, as nvkv_sample's Gumbel-max scores on this rank's vocab shard
+        and the vocab-parallel pick of the winner (no logits gathered).
+        temperatures [B] f32 on the device (<= 0: greedy)."""
+        local = self._local_logits(st)
+        v, gi = ops.sample(local, temperatures, seed, step, vocab_offset=self.rank * local.size(-1))
+        return gi if self.tp == 1 else vocab_parallel_pick(v, gi, self.group)
 
     def _local_logits(self, st: Step) -> torch.Tensor:
         """This rank's vocab shard of the last-token logits, [B, V/tp], model dtype."""

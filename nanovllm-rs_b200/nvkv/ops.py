@@ -11,7 +11,7 @@ from typing import Optional, Tuple
 
 import torch
 
-from ._lib import DTYPE_BF16, DTYPE_F16, NvkvError, ERR_INVALID_ARG, check, lib
+from ._lib import DTYPE_BF16, DTYPE_F16, DTYPE_F32, NvkvError, ERR_INVALID_ARG, check, lib
 
 _DT = {torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
 
@@ -255,6 +255,32 @@ def silu_and_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> t
     check(lib.nvkv_silu_and_mul(_ptr(gate_up), gate_up.stride(0), _ptr(out), out.stride(0), T, F,
                                 _dtype(gate_up), _stream()))
     return out
+
+
+def sample(logits: torch.Tensor, temperatures: torch.Tensor, seed: int, step: int,
+           vocab_offset: int = 0, out_value: Optional[torch.Tensor] = None,
+           out_index: Optional[torch.Tensor] = None):
+    """The reference's Sampler::forward (layers/sampler.rs:7-21) in its
+    Gumbel-max form, one launch: per row of `logits` [B, V] (bf16, f16 or
+    f32; a vocab-parallel shard whose column 0 is global index
+    `vocab_offset`), the score max_v logit / T - log(max(-log u, 1e-10)) and
+    its global index, u from Philox4x32-10 keyed by `seed` at counter (global
+    index / 4, row, step).  temperatures [B] f32 (<= 0: greedy).  Returns
+    (value [B] f32, index [B] int64); over shards, the largest value (ties to
+    the lowest index) is the row's token."""
+    _need(logits.dim() == 2 and logits.is_cuda and logits.stride(1) == 1, "logits: [B, V] rows")
+    B, V = logits.shape
+    dt = DTYPE_F32 if logits.dtype == torch.float32 else _dtype(logits)
+    _need(temperatures.dtype == torch.float32 and temperatures.numel() == B and
+          temperatures.is_contiguous(), "temperatures: f32 [B]")
+    if out_value is None:
+        out_value = torch.empty(B, dtype=torch.float32, device=logits.device)
+    if out_index is None:
+        out_index = torch.empty(B, dtype=torch.int64, device=logits.device)
+    check(lib.nvkv_sample(_ptr(logits), B, V, logits.stride(0), int(vocab_offset),
+                          _ptr(temperatures), int(seed) & (2**64 - 1), int(step) & (2**64 - 1),
+                          _ptr(out_value), _ptr(out_index), dt, _stream()))
+    return out_value, out_index
 
 
 def decode_advance(seq_lens: torch.Tensor, block_tables: torch.Tensor, num_blocks: int,

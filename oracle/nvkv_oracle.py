@@ -505,3 +505,75 @@ def dequantize_pages_fp8(cache, scales) -> np.ndarray:
     """[Nb, P, Hkv, D] codes + [Nb, Hkv, P] scales -> float32 values."""
     vals = e4m3_decode(cache)
     return (vals * np.transpose(scales, (0, 2, 1))[..., None]).astype(np.float32)
+
+
+# --------------------------------------------------------------------------
+# Sampler (layers/sampler.rs:7-21) and the counter-based noise of its
+# device form
+# --------------------------------------------------------------------------
+_PHILOX_M0, _PHILOX_M1 = 0xD2511F53, 0xCD9E8D57
+_PHILOX_W0, _PHILOX_W1 = 0x9E3779B9, 0xBB67AE85
+
+
+def philox4x32_10(ctr, key):
+    """Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC 2011; the Random123
+    definition): ctr [..., 4] uint32 words, key [2] uint32 words; ten rounds
+    of two 32x32->64 multiplies, key bumped by the Weyl constants between
+    rounds.  Returns [..., 4] uint32."""
+    c = [np.asarray(ctr[..., i], np.uint64) for i in range(4)]
+    k0, k1 = np.uint64(key[0]), np.uint64(key[1])
+    m32 = np.uint64(0xFFFFFFFF)
+    for _ in range(10):
+        p0 = np.uint64(_PHILOX_M0) * c[0]
+        p1 = np.uint64(_PHILOX_M1) * c[2]
+        c = [((p1 >> np.uint64(32)) ^ c[1] ^ k0) & m32, p1 & m32,
+             ((p0 >> np.uint64(32)) ^ c[3] ^ k1) & m32, p0 & m32]
+        k0 = (k0 + np.uint64(_PHILOX_W0)) & m32
+        k1 = (k1 + np.uint64(_PHILOX_W1)) & m32
+    return np.stack(c, -1).astype(np.uint32)
+
+
+def sample_uniforms(num_rows: int, vocab: int, seed: int, step: int, vocab_offset: int = 0):
+    """u [num_rows, vocab] f32 of the device sampler: Philox4x32-10 keyed by
+    the 64-bit seed at counter (global index // 4, row, step low, step high),
+    word global index % 4, u = ((bits >> 9) + 1/2) 2^-23."""
+    g = vocab_offset + np.arange(vocab, dtype=np.int64)
+    q0 = int(g[0] // 4) if vocab else 0
+    groups = np.arange(q0, int(g[-1] // 4) + 1 if vocab else q0, dtype=np.int64)
+    ctr = np.zeros((num_rows, len(groups), 4), np.uint64)
+    ctr[..., 0] = groups[None, :]
+    ctr[..., 1] = np.arange(num_rows, dtype=np.int64)[:, None]
+    ctr[..., 2] = step & 0xFFFFFFFF
+    ctr[..., 3] = (step >> 32) & 0xFFFFFFFF
+    bits = philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
+    word = bits[:, g // 4 - q0, g % 4]
+    return (((word >> np.uint32(9)).astype(np.float32) + np.float32(0.5)) *
+            np.float32(2.0 ** -23))
+
+
+def reference_sample(logits, temperatures, u):
+    """Sampler::forward (sampler.rs:7-21) given its uniforms u: softmax of the
+    f32 logits divided by the temperature, divided by max(-log u, 1e-10),
+    first arg-max."""
+    x = np.asarray(logits, np.float32) / np.asarray(temperatures, np.float32)[:, None]
+    x = x - x.max(-1, keepdims=True)
+    p = np.exp(x)
+    p = p / p.sum(-1, keepdims=True)
+    noise = np.maximum(-np.log(u.astype(np.float64)), 1e-10)
+    return np.argmax(p / noise, axis=-1)
+
+
+def gumbel_sample(logits, temperatures, seed: int, step: int, vocab_offset: int = 0):
+    """The device sampler's arithmetic (nvkv_sample): per row the largest
+    score logit / T - log(max(-log u, 1e-10)) in f32 and its global index
+    (first maximum); T <= 0 scores the logit itself.  Returns (value f32,
+    index int64)."""
+    x = np.asarray(logits, np.float32)
+    B, V = x.shape
+    t = np.asarray(temperatures, np.float32)
+    u = sample_uniforms(B, V, seed, step, vocab_offset)
+    e = np.maximum(-np.log(u), np.float32(1e-10)).astype(np.float32)
+    z = (x / np.where(t > 0, t, np.float32(1))[:, None]).astype(np.float32) - np.log(e)
+    z = np.where((t > 0)[:, None], z, x)
+    i = np.argmax(z, axis=-1)
+    return z[np.arange(B), i], i.astype(np.int64) + vocab_offset
