@@ -8,6 +8,9 @@
   tolerance (max-abs 2e-2, mean-abs 2e-3): decode batches (the split-KV plan
   and the one-wave plan, GQA groups up to 16) and mixed batches whose prompts
   are dequantised into the workspace and run through the tcgen05 prefill.
+* f16 queries (Q as three e4m3 pieces) and V rows scaled by 1e-4 and 3e3
+  (the decode keeps O in a running power-of-two unit) meet the same bar,
+  relative to the V scale.
 * A prompt whose keys do not fit prompt_kv_tokens is skipped and reported,
   its out rows untouched, the rest of the batch still correct.
 """
@@ -25,16 +28,17 @@ pytestmark = pytest.mark.gpu
 P, D = 256, 128
 
 
-def _pool(nb, hkv, seed, gain=None):
-    """An fp8 pool filled through nvkv_store_kvcache_fp8 from random bf16 rows;
-    returns (k, v, k_scale, v_scale) on the GPU and the dequantised pool."""
+def _pool(nb, hkv, seed, gain=None, dtype=torch.bfloat16, v_gain=1.0):
+    """An fp8 pool filled through nvkv_store_kvcache_fp8 from random rows of
+    `dtype`; returns (k, v, k_scale, v_scale) on the GPU and the dequantised
+    pool."""
     g = torch.Generator().manual_seed(seed)
     n = nb * P
     k = torch.randn(n, hkv, D, generator=g)
-    v = torch.randn(n, hkv, D, generator=g)
+    v = torch.randn(n, hkv, D, generator=g) * v_gain
     if gain is not None:
         k = k * gain(n)[:, None, None]
-    k, v = k.bfloat16().cuda(), v.bfloat16().cuda()
+    k, v = k.to(dtype).cuda(), v.to(dtype).cuda()
     kc = torch.zeros(nb, P, hkv, D, dtype=torch.uint8, device="cuda")
     vc = torch.zeros_like(kc)
     ks = torch.zeros(nb, hkv, P, dtype=torch.float32, device="cuda")
@@ -116,6 +120,30 @@ def test_decode_fp8_matches_oracle(lens, hq, hkv):
     for b in sorted(set(range(0, B, max(1, B // 16))) | {B - 1}):
         want = _want(qn[b:b + 1], kd, vd, tables[b], 1, lens[b], scale)
         assert_attention_close(out[b:b + 1], want, f"seq {b} len {lens[b]}")
+
+
+@pytest.mark.parametrize("dtype,v_gain", [(torch.float16, 1.0), (torch.bfloat16, 1e-4),
+                                          (torch.bfloat16, 3e3)])
+def test_decode_fp8_dtypes_and_value_ranges(dtype, v_gain):
+    """f16 queries (Q split into three e4m3 pieces) and V rows far below and
+    far above 1 (the running power-of-two unit of O must keep P' in range)."""
+    lens = np.random.default_rng(21).integers(100, 3000, 48).tolist()
+    hq, hkv = 8, 2
+    nb = sum((L + P - 1) // P for L in lens) + 2
+    pool, kd, vd = _pool(nb, hkv, seed=22, dtype=dtype, v_gain=v_gain)
+    tables, bt = _tables(lens, nb, seed=23)
+    g = torch.Generator().manual_seed(24)
+    B = len(lens)
+    q = (torch.randn(B, hq, D, generator=g) * 2).to(dtype).cuda()
+    scale = D ** -0.5
+    out = ops.paged_attention_fp8(q, *pool, cu([1] * B), cu(lens), bt, 1, max(lens), scale)
+    torch.cuda.synchronize()
+    assert nvkv.device_error() == 0
+    qn = f32(q)
+    for b in range(0, B, 3):
+        want = _want(qn[b:b + 1], kd, vd, tables[b], 1, lens[b], scale)
+        got = out[b:b + 1].float().cpu().numpy() / v_gain
+        assert_attention_close(torch.from_numpy(got), want / v_gain, f"seq {b} len {lens[b]}")
 
 
 def test_mixed_fp8_prompts_dequantised_into_workspace():
