@@ -438,19 +438,21 @@ def _timing_max(summary, world, dev):
     return summary
 
 
-def run_workload(model, world, dev, prompts, max_tokens, num_blocks, warm_prompts=None):
+def run_workload(model, world, dev, prompts, max_tokens, num_blocks, warm_prompts=None,
+                 kv_fp8=False):
     """Every prompt to completion through nvkv.engine (the reference's engine
     loop and scheduler defaults, greedy), on a fresh KV pool of `num_blocks`
-    pages; host-clock step times (schedule + metadata + H2D + model + D2H of
-    the tokens), worst rank.  `warm_prompts` run first, untimed, so library
-    warm-up (cuBLAS heuristics for the step shapes) stays out of the timing."""
+    pages (the fp8 pool with kv_fp8); host-clock step times (schedule +
+    metadata + H2D + model + D2H of the tokens), worst rank.  `warm_prompts`
+    run first, untimed, so library warm-up (cuBLAS heuristics for the step
+    shapes) stays out of the timing."""
     import torch
 
     from nvkv.engine import Engine
 
     model.k_caches, model.v_caches = [], []
     torch.cuda.empty_cache()
-    model.allocate_kv_cache(num_blocks, PAGE)
+    model.allocate_kv_cache(num_blocks, PAGE, kv_fp8=kv_fp8)
     if warm_prompts:
         eng = Engine(model, num_blocks, PAGE, max_num_batched_tokens=MAX_BATCHED)
         eng.generate(warm_prompts, 2)
@@ -467,19 +469,20 @@ def run_workload(model, world, dev, prompts, max_tokens, num_blocks, warm_prompt
     return summary, outs
 
 
-def workload_config4(model, world, dev):
+def workload_config4(model, world, dev, kv_fp8=False):
     """BASELINE config 4 end to end: 256 requests x 1024-token prompts of
     uniform random ids, 512 greedy tokens each, P=256, every step through the
     engine loop (prefill and mixed steps at the 16384-token budget, then
-    decode)."""
+    decode); kv_fp8 runs it over the optional fp8 (e4m3) pool."""
     rng = np.random.default_rng(41)
     V = model.cfg.vocab_size
     prompts = [rng.integers(0, V, PROMPT).tolist() for _ in range(NUM_SEQS)]
     warm = [rng.integers(0, V, PROMPT).tolist() for _ in range(MAX_BATCHED // PROMPT)]
     need = NUM_SEQS * ((PROMPT + MAX_OUT + PAGE - 1) // PAGE) + 16
-    s, _ = run_workload(model, world, dev, prompts, MAX_OUT, need, warm)
+    s, _ = run_workload(model, world, dev, prompts, MAX_OUT, need, warm, kv_fp8=kv_fp8)
     s["workload"] = ("config 4: Qwen3-8B, 256 requests x 1024-token prompts, 512 greedy tokens "
-                     "each, P=256, max_num_batched_tokens 16384, chunked prefill off")
+                     "each, P=256, max_num_batched_tokens 16384, chunked prefill off" +
+                     ("; fp8 (e4m3) KV pool, not the reference's format" if kv_fp8 else ""))
     return s
 
 
@@ -887,6 +890,7 @@ def run_nvkv(a):
     if not a.no_workloads:  # whole workloads through the engine loop (every rank)
         wl = {"config4": workload_config4(model, world, dev)}
         if world == 1:
+            wl["config4_kv_fp8"] = workload_config4(model, world, dev, kv_fp8=True)
             wl["config3_tp1"] = workload_config3(world, rank, dev, None)
             wl["config1"] = workload_config1(dev)
         elif world == 2:
