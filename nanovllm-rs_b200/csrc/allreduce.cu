@@ -59,7 +59,10 @@
 
 namespace nvkv {
 
-constexpr int kArCtas = 148;
+#ifndef NVKV_AR_CTAS
+#define NVKV_AR_CTAS 148
+#endif
+constexpr int kArCtas = NVKV_AR_CTAS;  // CTAs per call (rows are dealt to them round-robin)
 constexpr int kArMaxRanks = NVKV_COMM_MAX_RANKS;
 constexpr size_t kArLLMaxBytes = (size_t)4 << 20;  // messages up to 4 MiB take the LL form
 
