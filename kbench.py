@@ -187,6 +187,18 @@ def case_decode_fp8(name, lens, hq, hkv, nblocks, iters, copies=1):
                 bound="hbm", kv="e4m3 + f32 row scales")
 
 
+def case_sample(name, B, V, iters):
+    """nvkv_sample over [B, V] bf16 logits (a TP shard when V < 151936): one
+    read of the logits plus 2.5 Philox4x32-10 calls per 8 entries."""
+    lg = (torch.randn(B, V, device="cuda") * 3).bfloat16()
+    temps = torch.full((B,), 0.8, device="cuda")
+    v = torch.empty(B, dtype=torch.float32, device="cuda")
+    ix = torch.empty(B, dtype=torch.int64, device="cuda")
+    fn = lambda i: ops.sample(lg, temps, 7, i, out_value=v, out_index=ix)  # noqa: E731
+    med, _ = _time(fn, iters)
+    return dict(kernel=name, B=B, V=V, bytes=B * V * 2, s=med, bound="latency")
+
+
 def case_step_metadata(B, iters, P=256):
     """nvkv_decode_advance on a B-sequence decode step (lengths U[1025,1536],
     pages appended ahead): the device replacement of the host-side metadata
@@ -440,6 +452,8 @@ CASES = {
         8),
     "decode_32b_tp8_fp8": lambda it: case_decode_fp8(
         "decode_32b_tp8_fp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
+    "sample_8b_tp1": lambda it: case_sample("sample_8b_tp1", 256, 151936, it),
+    "sample_8b_tp8": lambda it: case_sample("sample_8b_tp8", 256, 151936 // 8, it),
     "prefill_8b": lambda it: case_prefill(it),
     "step_metadata": lambda it: case_step_metadata(256, it),
     "mixed_4b_tp1": lambda it: case_mixed(it, 1),
