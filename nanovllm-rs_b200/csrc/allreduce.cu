@@ -71,7 +71,7 @@ struct ArParams {
   int64_t region;              // bytes of one [max_tokens, hidden] buffer slot
   int64_t off_recv, off_gath, off_flag;
   int64_t ll_region;           // bytes of one LL [rows, hidden] slot (2 x the data)
-  int64_t off_recv_ll;
+  int64_t off_recv_ll, off_gath_ll;
   uint32_t* epoch;             // this rank's per-CTA epochs
   int rank, world;
   int two_shot;
@@ -129,6 +129,9 @@ __device__ __forceinline__ uint8_t* ar_gath(const ArParams& p, int q, int par, i
 
 // LL rows: 8-element vector c of a row (16 data bytes) is 4 words of 8 bytes,
 // data in the low half, the epoch in the high half.
+__device__ __forceinline__ uint8_t* ar_gath_ll(const ArParams& p, int q, int par, int64_t row) {
+  return p.base[q] + p.off_gath_ll + (int64_t)par * p.ll_region + row * p.H * 4;
+}
 __device__ __forceinline__ uint8_t* ar_recv_ll(const ArParams& p, int q, int par, int src,
                                                int64_t row) {
   return p.base[q] + p.off_recv_ll + ((int64_t)par * p.world + src) * p.ll_region +
@@ -364,28 +367,65 @@ __global__ void __launch_bounds__(kNormThreads) allreduce_rms_norm_ll_kernel(con
     return __ldcg(reinterpret_cast<const uint4*>(in + u * rb + (int64_t)c * 16));
   };
 
-  // ---- one-shot: push every row of this CTA to every peer, sum on arrival ----
-  for (int64_t u = b; u < p.T; u += kArCtas)
-    for (int c = tid; c < nvec; c += kNormThreads) {
-      const uint4 v = mine(u, c);
+  if (!p.two_shot) {
+    // ---- one-shot: push every row of this CTA to every peer, sum on arrival ----
+    for (int64_t u = b; u < p.T; u += kArCtas)
+      for (int c = tid; c < nvec; c += kNormThreads) {
+        const uint4 v = mine(u, c);
 #pragma unroll
-      for (int q = 0; q < kArMaxRanks; ++q)
-        if (q < W && q != r) st_ll(ar_recv_ll(p, q, par, r, u) + (int64_t)c * 32, v, e);
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < W && q != r) st_ll(ar_recv_ll(p, q, par, r, u) + (int64_t)c * 32, v, e);
+      }
+    for (int64_t u = b; u < p.T; u += kArCtas) {
+      T* ru = res + u * H;
+      norm_row_load<T>(
+          [&](int c) {
+            uint4 v[kArMaxRanks];
+#pragma unroll
+            for (int q = 0; q < kArMaxRanks; ++q)
+              if (q < W)
+                v[q] = q == r ? mine(u, c)
+                              : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
+                                      p.timeout_ns, fail, p.err);
+            return sum_vals<T>(v, W);
+          },
+          p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
     }
-  for (int64_t u = b; u < p.T; u += kArCtas) {
-    T* ru = res + u * H;
-    norm_row_load<T>(
-        [&](int c) {
-          uint4 v[kArMaxRanks];
+  } else {
+    // ---- two-shot, column-owned: rank o owns vectors [o nw, (o + 1) nw) of
+    // every row.  Every CTA pushes each of its rows' slices to their owners,
+    // sums the slice it owns over the ranks and pushes the sum to every rank,
+    // then normalises its rows from the gathered sums: both phases spread
+    // over all CTAs, each CTA exchanging with the CTAs of the same index ----
+    const int nw = nvec / W;  // vectors per owner (the host checks nvec % W == 0)
+    for (int64_t u = b; u < p.T; u += kArCtas)
+      for (int c = tid; c < nvec; c += kNormThreads) {
+        const int o = c / nw;
+        if (o != r) st_ll(ar_recv_ll(p, o, par, r, u) + (int64_t)c * 32, mine(u, c), e);
+      }
+    for (int64_t u = b; u < p.T; u += kArCtas)
+      for (int c = r * nw + tid; c < (r + 1) * nw; c += kNormThreads) {
+        uint4 v[kArMaxRanks];
 #pragma unroll
-          for (int q = 0; q < kArMaxRanks; ++q)
-            if (q < W)
-              v[q] = q == r ? mine(u, c)
-                            : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e,
-                                    p.timeout_ns, fail, p.err);
-          return sum_vals<T>(v, W);
-        },
-        p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < W)
+            v[q] = q == r ? mine(u, c)
+                          : ld_ll(ar_recv_ll(p, r, par, q, u) + (int64_t)c * 32, e, p.timeout_ns,
+                                  fail, p.err);
+        const uint4 sv = sum_vals<T>(v, W);
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < W) st_ll(ar_gath_ll(p, q, par, u) + (int64_t)c * 32, sv, e);
+      }
+    for (int64_t u = b; u < p.T; u += kArCtas) {
+      T* ru = res + u * H;
+      norm_row_load<T>(
+          [&](int c) {
+            return ld_ll(ar_gath_ll(p, r, par, u) + (int64_t)c * 32, e, p.timeout_ns, fail,
+                         p.err);
+          },
+          p.res_mode == NVKV_RESIDUAL_ADD ? ru : nullptr, ru, wt, p.eps, out + u * H, H, red);
+    }
   }
   __syncthreads();
   if (tid == 0 && !s_fail) p.epoch[b] = e;
@@ -420,14 +460,18 @@ size_t epoch_off(const nvkv_comm* c) { return flag_off(c) + round256(kFlagBytes)
 // LL slots hold 2 bytes of word per data byte, for messages up to kArLLMaxBytes
 size_t ll_region(const nvkv_comm* c) { return 2 * std::min(c->region, kArLLMaxBytes); }
 size_t recv_ll_off(const nvkv_comm* c) { return epoch_off(c) + round256(kEpochBytes); }
-size_t total_bytes(const nvkv_comm* c) {
+size_t gath_ll_off(const nvkv_comm* c) {
   return recv_ll_off(c) + 2 * (size_t)c->world * ll_region(c);
 }
+size_t total_bytes(const nvkv_comm* c) { return gath_ll_off(c) + 2 * ll_region(c); }
 
 // One-shot (every rank pushes its whole partial to every peer, one barrier)
 // for two ranks; two-shot (push to the row's owner, owner reduces and
 // broadcasts, two barriers, 2 (n - 1) / n of the bytes) above.
 // NVKV_AR_TWO_SHOT_MIN_RANKS moves the switch (tuning builds).
+#ifndef NVKV_AR_LL_TWO_SHOT
+#define NVKV_AR_LL_TWO_SHOT 0
+#endif
 #ifndef NVKV_AR_TWO_SHOT_MIN_RANKS
 #define NVKV_AR_TWO_SHOT_MIN_RANKS 3
 #endif
@@ -568,6 +612,7 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   p.off_flag = (int64_t)flag_off(c);
   p.ll_region = (int64_t)ll_region(c);
   p.off_recv_ll = (int64_t)recv_ll_off(c);
+  p.off_gath_ll = (int64_t)gath_ll_off(c);
   p.epoch = reinterpret_cast<uint32_t*>(c->base + epoch_off(c));
   p.rank = c->rank;
   p.world = c->world;
@@ -585,10 +630,11 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   p.err = device_error_word();
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // every rank sees the same num_tokens, so every rank takes the same form.
-  // LL only for the one-shot protocol: its words double the bytes pushed,
-  // which two-shot at 8 ranks paid for (33.5 us per 2 MiB call against 24.4
-  // with the flag hand-off), while two ranks gain (15.8 us, NCCL 28.2).
-  const bool ll = !p.two_shot && (size_t)num_tokens * (size_t)hidden * 2 <= kArLLMaxBytes;
+  // LL for the one-shot protocol (two ranks: 15.8 us per 2 MiB call, NCCL
+  // 28.2) and, with NVKV_AR_LL_TWO_SHOT, for the column-owned two-shot one
+  // (the hidden size's 8-element vectors must split evenly over the ranks).
+  const bool small = (size_t)num_tokens * (size_t)hidden * 2 <= kArLLMaxBytes;
+  const bool ll = small && (!p.two_shot || (NVKV_AR_LL_TWO_SHOT && (hidden / 8) % c->world == 0));
   if (dtype == NVKV_DTYPE_BF16) {
     if (ll)
       allreduce_rms_norm_ll_kernel<__nv_bfloat16><<<kArCtas, kNormThreads, 0, s>>>(p);
