@@ -6,10 +6,10 @@
 // chunk of one sequence's keys for ONE kv head and serves all g = Hq/Hkv
 // query heads of that group, so every K/V byte leaves HBM once per group.
 //
-//  * warp 4 (one elected lane) is the TMA producer: per 64-token tile it
-//    resolves the page through block_tables, then issues four
-//    cp.async.bulk.tensor loads (K and V, two 64-element halves of the
-//    128-wide head each, SWIZZLE_128B) into a 3-stage mbarrier ring;
+//  * warp 4 is the TMA producer: it reads the chunk's block-table entries 32
+//    pages at a time (one coalesced load), and one lane issues, per 64-token
+//    tile, four cp.async.bulk.tensor loads (K and V, two 64-element halves of
+//    the 128-wide head each, SWIZZLE_128B) into a 3-stage mbarrier ring;
 //  * warps 0-3 each own 16 tokens of every tile: S = Q.K^T and O += P.V run
 //    on m16n8k16 MMAs (rows = the g query heads, padded to 16), the online
 //    softmax is fp32 with quad shuffles, and P never leaves registers (the S
@@ -20,6 +20,10 @@
 //
 // Roofline: HBM.  Algorithmic bytes per (sequence, kv head) = 2*L*D*2 (K, V)
 // plus q/out rows; nothing is re-read across query heads.
+//
+// The fp8 (e4m3) pool runs the same kernel with kFp8 = true: 128-key tiles
+// of codes and row scales, and the transposed e4m3 / f16 products of
+// dec8_tile (decode_tile.cuh); see the constants below.
 #include <algorithm>
 
 #include "decode_tile.cuh"
@@ -57,9 +61,10 @@ struct DecodeParams {
 // fp8 (e4m3) pool: 128-key tiles.  The producer stages each tile's K and V
 // codes (128 rows x 128 B, one TMA box each, SWIZZLE_128B) and the tile's
 // 128 K and 128 V row scales (two 512-byte bulk copies from [page][kv head]
-// [row]) in a 3-stage ring, two CTAs per SM; each compute warp runs the transposed e4m3 / f16
-// products of dec8_tile on 32 keys of every tile, on the codes in place, so
-// HBM and shared memory each see half the bf16 K/V bytes.  A tile carries as
+// [row]) in a 3-stage ring, two CTAs per SM; each compute warp runs the
+// transposed e4m3 / f16 products of dec8_tile on 32 keys of every tile, on
+// the codes in place, so HBM and shared memory each see half the bf16 K/V
+// bytes.  A tile carries as
 // many bytes as a 64-key bf16 tile: the per-tile costs of the copy pipeline
 // (measured to bound 64-key fp8 tiles well below the HBM peak) stay the
 // same per byte.
