@@ -27,7 +27,7 @@
 
 namespace nvkv {
 
-constexpr int kSampThreads = 256;
+constexpr int kSampThreads = 1024;  // one row per CTA: enough warps to hide the Philox chains
 
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
 #pragma unroll
