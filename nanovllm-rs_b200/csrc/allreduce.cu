@@ -36,9 +36,12 @@
 // locally.
 //
 // Small messages (at most kArLLMaxBytes, e.g. a decode step's 256 x 4096
-// rows) between two ranks take the low-latency (LL) form of the one-shot
-// protocol instead (a two-shot LL form measured slower than the flag
-// hand-off at 8 ranks, 33.5 against 24.4 us per 2 MiB call, and was removed):
+// rows) take the low-latency (LL) form instead: one-shot between two ranks;
+// above, a column-owned two-shot (rank o owns a slice of every row's
+// columns, so both phases spread over all CTAs -- a row-owned LL two-shot,
+// whose owner phase ran on the few CTAs holding a rank's rows, measured
+// slower than the flag hand-off at 8 ranks, 33.5 against 24.4 us per 2 MiB
+// call, and was removed):
 // every 8-byte word pushed to a peer carries 4 bytes of data and the call's
 // epoch in its upper half, stored and polled as single-copy-atomic 64-bit
 // words (st/ld.relaxed.sys).  The receiver spins on the words themselves, so
@@ -469,8 +472,12 @@ size_t total_bytes(const nvkv_comm* c) { return gath_ll_off(c) + 2 * ll_region(c
 // for two ranks; two-shot (push to the row's owner, owner reduces and
 // broadcasts, two barriers, 2 (n - 1) / n of the bytes) above.
 // NVKV_AR_TWO_SHOT_MIN_RANKS moves the switch (tuning builds).
+// LL form for the two-shot protocol too (column-owned).  Measured with the
+// two-shot protocol forced at two ranks (2 MiB / 512 KiB / 128 KiB calls):
+// 15.0 / 8.0 / 7.2 us against 18.5 / 15.2 / 14.3 for the flag hand-off and
+// 15.2 / 7.9 / 6.3 for the one-shot LL form, bit-identical results.
 #ifndef NVKV_AR_LL_TWO_SHOT
-#define NVKV_AR_LL_TWO_SHOT 0
+#define NVKV_AR_LL_TWO_SHOT 1
 #endif
 #ifndef NVKV_AR_TWO_SHOT_MIN_RANKS
 #define NVKV_AR_TWO_SHOT_MIN_RANKS 3
@@ -631,8 +638,8 @@ extern "C" int nvkv_allreduce_rms_norm(nvkv_comm_t c, int64_t num_tokens, int hi
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // every rank sees the same num_tokens, so every rank takes the same form.
   // LL for the one-shot protocol (two ranks: 15.8 us per 2 MiB call, NCCL
-  // 28.2) and, with NVKV_AR_LL_TWO_SHOT, for the column-owned two-shot one
-  // (the hidden size's 8-element vectors must split evenly over the ranks).
+  // 28.2) and for the column-owned two-shot one (NVKV_AR_LL_TWO_SHOT; the
+  // hidden size's 8-element vectors must split evenly over the ranks).
   const bool small = (size_t)num_tokens * (size_t)hidden * 2 <= kArLLMaxBytes;
   const bool ll = small && (!p.two_shot || (NVKV_AR_LL_TWO_SHOT && (hidden / 8) % c->world == 0));
   if (dtype == NVKV_DTYPE_BF16) {
