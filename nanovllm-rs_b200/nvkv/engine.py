@@ -15,16 +15,20 @@ nvkv kernels.  It follows the reference's engine loop:
     pool allow (so prompts and decodes share a step);
   * Scheduler::postprocess (scheduler.rs:53-96): append the sampled token,
     finish on max_tokens / EOS / max_model_len and free the blocks;
-  * sampling is greedy (the temperature -> 0 limit of sampler.rs:7-21).
+  * sampling: each request's temperature (SamplingParams, sampling_params.rs)
+    goes to the device sampler (nvkv_sample, the Gumbel-max form of
+    sampler.rs:7-21) with the engine's seed and a step counter; temperature
+    0 (the default here, as the benchmarks decode greedily) is the greedy
+    pick, the temperature -> 0 limit.
 
 Each sequence keeps one C view (nvkv_block_seq) over buffers it owns for its
 whole life (token ids up to prompt + max_tokens, its block table), so a step
 marshals nothing per token: one append_batch call for the running queue, one
 prepare_step call for the step's metadata, written into pinned host buffers
 and copied to the device in one batch of copies.  All ranks of a TP group run
-the same loop on the same inputs; the greedy tokens are identical on every
-rank (vocab-parallel argmax), so the ranks stay in lockstep without a
-broadcast.
+the same loop on the same inputs; the tokens are identical on every rank
+(the vocab-parallel pick over the ranks' candidates, the same seed and step
+on every rank), so the ranks stay in lockstep without a broadcast.
 """
 from __future__ import annotations
 
@@ -44,10 +48,13 @@ from .decoder import Step
 class _Seq:
     """One request: Sequence (engine/sequence.rs) fields the loop needs."""
 
-    __slots__ = ("sid", "tokens", "table", "c", "num_prompt", "max_tokens", "ignore_eos")
+    __slots__ = ("sid", "tokens", "table", "c", "num_prompt", "max_tokens", "ignore_eos",
+                 "temperature")
 
-    def __init__(self, sid: int, prompt, max_tokens: int, block_size: int, ignore_eos: bool):
+    def __init__(self, sid: int, prompt, max_tokens: int, block_size: int, ignore_eos: bool,
+                 temperature: float = 0.0):
         self.sid = sid
+        self.temperature = float(temperature)
         self.num_prompt = len(prompt)
         self.max_tokens = max_tokens
         self.ignore_eos = ignore_eos
@@ -72,8 +79,10 @@ class Engine:
 
     def __init__(self, model, num_blocks: int, block_size: int = 256, max_num_seqs: int = 512,
                  max_num_batched_tokens: int = 16384, max_model_len: int = 40960,
-                 eos: int = -1, cuda_graphs: bool = True):
+                 eos: int = -1, cuda_graphs: bool = True, seed: int = 0):
         self.model = model
+        self.seed = int(seed)
+        self._step_no = 0  # the sampler's counter: one per engine step
         self.block_size = block_size
         self.max_num_seqs = max_num_seqs
         self.budget = max_num_batched_tokens
@@ -99,6 +108,8 @@ class Engine:
                       bt=torch.zeros(B * self._w, dtype=torch.int32, **pin))
         self.d = {k: torch.zeros(v.numel(), dtype=v.dtype, device=dev) for k, v in self.h.items()}
         self.tok_h = torch.zeros(B, dtype=torch.int64, **pin)
+        self.temp_h = torch.zeros(B, dtype=torch.float32, **pin)
+        self.temp_d = torch.zeros(B, dtype=torch.float32, device=dev)
         self.stats = []  # per step: (prompt tokens, decode tokens, seconds)
         # pure decode steps replay a CUDA graph per (batch size, context bucket);
         # a key is captured when it repeats on consecutive steps (config-4-like
@@ -117,11 +128,15 @@ class Engine:
         self.bm.close()
 
     # ---- requests ----------------------------------------------------------
-    def add_request(self, prompt, max_tokens: int, ignore_eos: bool = True) -> int:
-        """LLMEngine::add_request + Scheduler::add (scheduler.rs:40-46)."""
+    def add_request(self, prompt, max_tokens: int, ignore_eos: bool = True,
+                    temperature: float = 0.0) -> int:
+        """LLMEngine::add_request + Scheduler::add (scheduler.rs:40-46);
+        temperature 0 decodes greedily."""
         if len(prompt) > self.max_model_len - 1:
             raise ValueError("Sequence length exceeds max_model_len")
-        s = _Seq(self._next, prompt, max_tokens, self.block_size, ignore_eos)
+        if temperature < 0:
+            raise ValueError("temperature must be >= 0")
+        s = _Seq(self._next, prompt, max_tokens, self.block_size, ignore_eos, temperature)
         self._next += 1
         self.waiting.append(s)
         return s.sid
@@ -240,14 +255,22 @@ class Engine:
         prompt_tok = sum(int(s.c.num_new_tokens) for s in sched if s.c.num_new_tokens > 1)
         decode_tok = sum(1 for s in sched if s.c.num_new_tokens == 1)
         st = self._prepare(sched)
-        tok = self._decode_graph(st) if self.cuda_graphs and self._decode_only else None
-        if tok is None:
-            tok = self.model.greedy(st)
         n = self._n_need
+        need = self.h["need"][:n].tolist()
+        temps = [sched[i].temperature for i in need]
+        step_no = self._step_no
+        self._step_no += 1
+        if any(t > 0 for t in temps):  # the logits rows' temperatures (0: greedy rows)
+            self.temp_h[:n] = torch.tensor(temps, dtype=torch.float32)
+            self.temp_d[:n].copy_(self.temp_h[:n], non_blocking=self._cuda)
+            tok = self.model.sample(st, self.temp_d[:n], self.seed, step_no)
+        else:
+            tok = self._decode_graph(st) if self.cuda_graphs and self._decode_only else None
+            if tok is None:
+                tok = self.model.greedy(st)
         self.tok_h[:n].copy_(tok[:n], non_blocking=self._cuda)
         if self._cuda:
             torch.cuda.current_stream().synchronize()
-        need = self.h["need"][:n].tolist()
         toks = self.tok_h[:n].tolist()
         for idx, t in zip(need, toks):  # postprocess (scheduler.rs:53-96)
             s = sched[idx]
@@ -316,10 +339,14 @@ class Engine:
         self.graph_steps += 1
         return g[1]
 
-    def generate(self, prompts, max_tokens: int, ignore_eos: bool = True) -> List[List[int]]:
+    def generate(self, prompts, max_tokens: int, ignore_eos: bool = True,
+                 temperature=0.0) -> List[List[int]]:
         """LLMEngine::generate: every prompt to completion; the completions in
-        request order."""
-        ids = [self.add_request(p, max_tokens, ignore_eos) for p in prompts]
+        request order.  temperature: one value for every request or one per
+        prompt."""
+        temps = (list(temperature) if isinstance(temperature, (list, tuple))
+                 else [temperature] * len(prompts))
+        ids = [self.add_request(p, max_tokens, ignore_eos, t) for p, t in zip(prompts, temps)]
         while not self.is_finished():
             self.step()
         return [self.finished[i] for i in ids]

@@ -11,6 +11,8 @@ over the oracle's BlockManager and prepare_model_input, and its sampled
 token is computed from the oracle's own step inputs.  Both must give the
 same completions, the same number of steps and the same per-step prompt /
 decode token counts, including on pools small enough to preempt.
+Per-request temperatures reach the model's sample() with the engine's seed
+and step counter, row by row, and greedy rows stay greedy.
 """
 from collections import deque
 
@@ -27,6 +29,14 @@ V = 1000
 
 def _token(ids_last, pos_last):
     return (int(ids_last) * 31 + int(pos_last) * 7 + 3) % V
+
+
+def _sampled(ids_last, pos_last, temp, seed, step):
+    """The stand-in's sampled token: the greedy one for temperature 0, else a
+    fixed function of the temperature, the seed and the step counter too."""
+    if temp <= 0:
+        return _token(ids_last, pos_last)
+    return (_token(ids_last, pos_last) + int(round(temp * 10)) + 13 * seed + 101 * step) % V
 
 
 class _FakeModel:
@@ -52,9 +62,22 @@ class _FakeModel:
                 assert int(st.slot_mapping[t]) == want
         return torch.tensor([_token(ids[r], pos[r]) for r in last], dtype=torch.int64)
 
+    def sample(self, st, temps, seed, step):
+        greedy = self.greedy(st).numpy()  # the same metadata checks
+        ids, pos = st.input_ids.numpy(), st.positions.numpy()
+        last = st.last_idx.numpy()
+        t = temps.numpy()
+        assert len(t) == len(last)
+        out = [_sampled(ids[r], pos[r], float(t[k]), seed, step) for k, r in enumerate(last)]
+        assert all(o == g for o, g, tk in zip(out, greedy, t) if tk <= 0)
+        return torch.tensor(out, dtype=torch.int64)
 
-def _reference(prompts, max_tokens, num_blocks, page, budget, max_seqs):
-    """LLMEngine::generate with Scheduler (non-chunked) on the oracle pieces."""
+
+def _reference(prompts, max_tokens, num_blocks, page, budget, max_seqs, temps=None, seed=0):
+    """LLMEngine::generate with Scheduler (non-chunked) on the oracle pieces;
+    temps: per-request temperatures (None: greedy)."""
+    temps = temps or [0.0] * len(prompts)
+    step_no = 0
     bm = OB.BlockManager(num_blocks, page)
     waiting = deque((i, OB.Seq(list(p), page)) for i, p in enumerate(prompts))
     running = deque()
@@ -102,7 +125,7 @@ def _reference(prompts, max_tokens, num_blocks, page, budget, max_seqs):
         last = ctx.cu_seqlens_q[1:].astype(np.int64) - 1
         for k in ctx.seq_need_compute_logits:  # scheduler.rs:53-96
             sid, s = sched[k]
-            t = _token(ids[last[k]], pos[last[k]])
+            t = _sampled(ids[last[k]], pos[last[k]], temps[sid], seed, step_no)
             s.append_token(t)
             if len(s) - len(prompts[sid]) >= max_tokens:
                 bm.deallocate(s)
@@ -111,6 +134,7 @@ def _reference(prompts, max_tokens, num_blocks, page, budget, max_seqs):
             else:
                 s.num_cached_tokens += s.num_new_tokens
                 s.num_new_tokens = 0
+        step_no += 1
     return [done[i] for i in range(len(prompts))], stats
 
 
@@ -133,4 +157,23 @@ def test_engine_matches_reference_loop(seed, page, num_blocks, budget, max_seqs)
     assert eng.bm.num_free == num_blocks  # every block returned
     s = eng.summary()
     assert s["generated_tokens"] == 12 * max_tokens
+    eng.close()
+
+
+def test_engine_temperatures_go_to_the_sampler():
+    """Per-request temperatures: rows with T > 0 are sampled (the model's
+    sample() with the engine's seed and step counter), T = 0 rows stay
+    greedy, and a step with only greedy rows takes the greedy path."""
+    rng = np.random.default_rng(7)
+    prompts = [rng.integers(0, V, int(L)).tolist() for L in rng.integers(1, 60, 10)]
+    temps = [0.0, 0.7, 1.0, 0.0, 1.3, 0.2, 0.0, 0.9, 0.0, 2.0]
+    want, _ = _reference(prompts, 15, 400, 16, 256, 512, temps=temps, seed=5)
+    eng = Engine(_FakeModel(16), 400, 16, max_num_batched_tokens=256, max_model_len=4096,
+                 seed=5)
+    assert eng.generate(prompts, 15, temperature=temps) == want
+    eng.close()
+    greedy, _ = _reference(prompts, 15, 400, 16, 256, 512)
+    assert want != greedy  # the sampled rows changed something
+    eng = Engine(_FakeModel(16), 400, 16, max_num_batched_tokens=256, max_model_len=4096)
+    assert eng.generate(prompts, 15) == greedy
     eng.close()
