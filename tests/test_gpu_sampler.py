@@ -13,6 +13,8 @@ distribution the reference samples from.
   5 standard deviations.
 * The Qwen3 driver's sample() equals nvkv_sample over its own logits, and is
   greedy at T = 0.
+* The serving loop with per-request temperatures is reproducible for a seed,
+  and its T = 0 requests match the greedy completions.
 """
 import numpy as np
 import pytest
@@ -124,4 +126,32 @@ def test_decoder_sample():
     assert torch.equal(tok, want)
     assert torch.equal(model.sample(st, torch.zeros(B, device="cuda"), 5, 0),
                        logits.argmax(-1))
+    assert nvkv.device_error() == 0
+
+
+def test_engine_sampling_is_reproducible():
+    """The serving loop with per-request temperatures on the GPU: the same
+    seed gives the same completions, another seed other ones, and
+    temperature 0 gives the greedy completions."""
+    import test_gpu_greedy as G
+    from nvkv.decoder import Qwen3TP
+    from nvkv.engine import Engine
+    model = Qwen3TP(G.CFG, seed=3, device="cuda", **G.INIT)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, G.CFG.vocab_size, int(L)).tolist() for L in (40, 97, 130, 64)]
+
+    def run(temps, seed):
+        model.allocate_kv_cache(12, G.P)
+        eng = Engine(model, 12, G.P, max_num_batched_tokens=1024, max_model_len=4096, seed=seed)
+        out = eng.generate(prompts, 10, temperature=temps)
+        eng.close()
+        return out
+
+    a = run([1.0, 0.8, 1.2, 0.5], 1)
+    assert a == run([1.0, 0.8, 1.2, 0.5], 1)
+    assert a != run([1.0, 0.8, 1.2, 0.5], 2)
+    mixed = run([0.0, 0.8, 0.0, 0.5], 1)
+    greedy = run(0.0, 1)
+    assert mixed[0] == greedy[0] and mixed[2] == greedy[2]
+    assert all(0 <= t < G.CFG.vocab_size for c in a for t in c)
     assert nvkv.device_error() == 0
