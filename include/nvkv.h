@@ -284,7 +284,10 @@ int nvkv_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, in
  * (vocab_offset = the global index of its column 0) gives the same
  * candidates as the whole vocabulary, and the largest value over the shards
  * (ties to the lowest index) is the whole row's sample.  Temperatures <= 0
- * give the plain arg-max (greedy).
+ * give the plain arg-max (greedy).  The counter's step is `step` plus, when
+ * step_device is not NULL, the int64 it points to (device memory, read by
+ * the kernel): a CUDA graph that replays the call sets that word between
+ * replays.
  * logits: [num_rows, row_stride] of dtype NVKV_DTYPE_BF16 / F16 / F32 (the
  * first `vocab` columns are read); temperatures [num_rows] f32; out_value
  * [num_rows] f32 (the winning score), out_index [num_rows] i64 (its global
@@ -292,7 +295,8 @@ int nvkv_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, in
  * ---------------------------------------------------------------------- */
 int nvkv_sample(const void* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
                 int64_t vocab_offset, const float* temperatures, uint64_t seed, uint64_t step,
-                float* out_value, int64_t* out_index, int dtype, nvkv_stream_t stream);
+                const int64_t* step_device, float* out_value, int64_t* out_index, int dtype,
+                nvkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Device-side metadata of a pure decode step.  Replaces the decode case of

@@ -90,13 +90,15 @@ template <typename T>
 __global__ void __launch_bounds__(kSampThreads)
     sample_kernel(const T* __restrict__ logits, int64_t vocab, int64_t row_stride,
                   int64_t vocab_offset, const float* __restrict__ temps, uint32_t k0, uint32_t k1,
-                  uint32_t step_lo, uint32_t step_hi, float* __restrict__ out_value,
-                  int64_t* __restrict__ out_index) {
+                  uint64_t step0, const int64_t* __restrict__ step_ptr,
+                  float* __restrict__ out_value, int64_t* __restrict__ out_index) {
   __shared__ float sv[kSampThreads / 32];
   __shared__ int64_t si[kSampThreads / 32];
   const int64_t b = blockIdx.x;
   const T* row = logits + b * row_stride;
   const float temp = temps[b];
+  const uint64_t step = step0 + (step_ptr ? (uint64_t)*step_ptr : 0ull);
+  const uint32_t step_lo = (uint32_t)step, step_hi = (uint32_t)(step >> 32);
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
   // vectors of 8 where the row allows them (16-byte aligned row, offset a
@@ -148,8 +150,9 @@ __global__ void __launch_bounds__(kSampThreads)
 
 extern "C" int nvkv_sample(const void* logits, int64_t num_rows, int64_t vocab,
                            int64_t row_stride, int64_t vocab_offset, const float* temperatures,
-                           uint64_t seed, uint64_t step, float* out_value, int64_t* out_index,
-                           int dtype, nvkv_stream_t stream) {
+                           uint64_t seed, uint64_t step, const int64_t* step_device,
+                           float* out_value, int64_t* out_index, int dtype,
+                           nvkv_stream_t stream) {
   NVKV_RANGE("nvkv_sample");
   using namespace nvkv;
   clear_error();
@@ -164,20 +167,19 @@ extern "C" int nvkv_sample(const void* logits, int64_t num_rows, int64_t vocab,
   if (dtype != NVKV_DTYPE_BF16 && dtype != NVKV_DTYPE_F16 && dtype != NVKV_DTYPE_F32)
     return set_error(NVKV_ERR_UNSUPPORTED, "sample: logits must be bf16, f16 or f32");
   const uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
-  const uint32_t s0 = (uint32_t)step, s1 = (uint32_t)(step >> 32);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)num_rows);
   if (dtype == NVKV_DTYPE_BF16)
     sample_kernel<__nv_bfloat16><<<grid, kSampThreads, 0, s>>>(
         static_cast<const __nv_bfloat16*>(logits), vocab, row_stride, vocab_offset, temperatures,
-        k0, k1, s0, s1, out_value, out_index);
+        k0, k1, step, step_device, out_value, out_index);
   else if (dtype == NVKV_DTYPE_F16)
     sample_kernel<__half><<<grid, kSampThreads, 0, s>>>(static_cast<const __half*>(logits), vocab,
                                                         row_stride, vocab_offset, temperatures, k0,
-                                                        k1, s0, s1, out_value, out_index);
+                                                        k1, step, step_device, out_value, out_index);
   else
     sample_kernel<float><<<grid, kSampThreads, 0, s>>>(static_cast<const float*>(logits), vocab,
                                                        row_stride, vocab_offset, temperatures, k0,
-                                                       k1, s0, s1, out_value, out_index);
+                                                       k1, step, step_device, out_value, out_index);
   return check_cuda(cudaGetLastError(), "sample launch");
 }

@@ -91,7 +91,7 @@ SIGNATURES = {
     "nvkv_silu_and_mul": [_p, _i64, _p, _i64, _i64, _i32, _i32, _p],
     "nvkv_decode_advance": [_i32, _i32, _p, _p, _i64, _i64, _p, _p, _p, _p, _p],
     "nvkv_sample": [_p, _i64, _i64, _i64, _i64, _p, ctypes.c_uint64, ctypes.c_uint64, _p, _p,
-                    _i32, _p],
+                    _p, _i32, _p],
     "nvkv_comm_create": [_i32, _i32, _sz, ctypes.POINTER(_p), _p],
     "nvkv_comm_open_peers": [_p, _p],
     "nvkv_comm_input": [_p, ctypes.POINTER(_p)],

@@ -323,14 +323,17 @@ class Qwen3TP:
             return local.argmax(dim=-1)
         return vocab_parallel_argmax(local, self.rank, self.group)
 
-    def sample(self, st: Step, temperatures: torch.Tensor, seed: int, step: int) -> torch.Tensor:
+    def sample(self, st: Step, temperatures: torch.Tensor, seed: int, step: int,
+               step_device: Optional[torch.Tensor] = None) -> torch.Tensor:
         """The sampled next token of every sequence, [B] int64: the
         reference's Sampler::forward (layers/sampler.rs:7-21) over forward()'s
         logits, as nvkv_sample's Gumbel-max scores on this rank's vocab shard
         and the vocab-parallel pick of the winner (no logits gathered).
-        temperatures [B] f32 on the device (<= 0: greedy)."""
+        temperatures [B] f32 on the device (<= 0: greedy); step_device: an
+        int64 [1] device counter added to `step` (for graph replays)."""
         local = self._local_logits(st)
-        v, gi = ops.sample(local, temperatures, seed, step, vocab_offset=self.rank * local.size(-1))
+        v, gi = ops.sample(local, temperatures, seed, step, vocab_offset=self.rank * local.size(-1),
+                           step_device=step_device)
         return gi if self.tp == 1 else vocab_parallel_pick(v, gi, self.group)
 
     def _local_logits(self, st: Step) -> torch.Tensor:

@@ -110,6 +110,7 @@ class Engine:
         self.tok_h = torch.zeros(B, dtype=torch.int64, **pin)
         self.temp_h = torch.zeros(B, dtype=torch.float32, **pin)
         self.temp_d = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.step_d = torch.zeros(1, dtype=torch.int64, device=dev)  # sampler counter (graphs)
         self.stats = []  # per step: (prompt tokens, decode tokens, seconds)
         # pure decode steps replay a CUDA graph per (batch size, context bucket);
         # a key is captured when it repeats on consecutive steps (config-4-like
@@ -260,14 +261,16 @@ class Engine:
         temps = [sched[i].temperature for i in need]
         step_no = self._step_no
         self._step_no += 1
-        if any(t > 0 for t in temps):  # the logits rows' temperatures (0: greedy rows)
+        sampling = any(t > 0 for t in temps)  # the logits rows' temperatures (0: greedy)
+        if sampling:
             self.temp_h[:n] = torch.tensor(temps, dtype=torch.float32)
             self.temp_d[:n].copy_(self.temp_h[:n], non_blocking=self._cuda)
-            tok = self.model.sample(st, self.temp_d[:n], self.seed, step_no)
-        else:
-            tok = self._decode_graph(st) if self.cuda_graphs and self._decode_only else None
-            if tok is None:
-                tok = self.model.greedy(st)
+        tok = None
+        if self.cuda_graphs and self._decode_only:
+            tok = self._decode_graph(st, step_no if sampling else None)
+        if tok is None:
+            tok = (self.model.sample(st, self.temp_d[:n], self.seed, step_no) if sampling
+                   else self.model.greedy(st))
         self.tok_h[:n].copy_(tok[:n], non_blocking=self._cuda)
         if self._cuda:
             torch.cuda.current_stream().synchronize()
@@ -293,15 +296,19 @@ class Engine:
         self.stats.append((prompt_tok, decode_tok, time.perf_counter() - t0))
         return n
 
-    def _decode_graph(self, st: Step) -> Optional[torch.Tensor]:
+    def _decode_graph(self, st: Step, step_no: Optional[int] = None) -> Optional[torch.Tensor]:
         """A pure decode step through a captured CUDA graph, or None (then the
         step runs eagerly).  The graph's step has fixed shapes: the batch size,
         max_seqlen_k rounded up to a multiple of 1024 (the kernels take it as a
         bound) and block tables padded to that many pages in a fixed buffer;
-        the step's own metadata is copied into the same device buffers first."""
+        the step's own metadata is copied into the same device buffers first.
+        With step_no (a sampling step) the graph samples with the rows'
+        temperatures from temp_d and the counter from step_d, both set before
+        each replay, so replays draw exactly the eager step's noise."""
         B, P = self._B, self.block_size
         bucket = -(-self._max_k // 1024) * 1024
-        key = (B, bucket)
+        sampling = step_no is not None
+        key = (B, bucket, sampling)
         g = self._graphs.get(key)
         if g is None and (self._last_key != key or len(self._graphs) >= 8):
             self._last_key = key
@@ -315,12 +322,20 @@ class Engine:
         d = self.d
         stg = Step(d["ids"][:B], d["pos"][:B], d["slots"][:B], d["cu_q"][:B + 1],
                    d["cu_k"][:B + 1], self.d_bt_g[:B * Wg].view(B, Wg), st.last_idx, 1, bucket, 0)
+        if sampling:
+            self.step_d.fill_(step_no)
+            temps = self.temp_d[:B]
+
+            def pick(s):
+                return self.model.sample(s, temps, self.seed, 0, step_device=self.step_d)
+        else:
+            pick = self.model.greedy
         if g is None:  # capture: one eager warm-up of these shapes, then the graph
-            self.model.greedy(stg)
+            pick(stg)
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(side):
-                self.model.greedy(stg)
+                pick(stg)
             torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
             last = d["need"][:B]
@@ -331,7 +346,7 @@ class Engine:
             try:
                 with torch.cuda.graph(graph):
                     stg.last_idx = d["cu_q"].index_select(0, last + 1).long() - 1
-                    out = self.model.greedy(stg)
+                    out = pick(stg)
             finally:
                 self.model._bufs = saved
             g = self._graphs[key] = (graph, out)

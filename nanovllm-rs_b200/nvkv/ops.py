@@ -259,13 +259,15 @@ def silu_and_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> t
 
 def sample(logits: torch.Tensor, temperatures: torch.Tensor, seed: int, step: int,
            vocab_offset: int = 0, out_value: Optional[torch.Tensor] = None,
-           out_index: Optional[torch.Tensor] = None):
+           out_index: Optional[torch.Tensor] = None, step_device: Optional[torch.Tensor] = None):
     """The reference's Sampler::forward (layers/sampler.rs:7-21) in its
     Gumbel-max form, one launch: per row of `logits` [B, V] (bf16, f16 or
     f32; a vocab-parallel shard whose column 0 is global index
     `vocab_offset`), the score max_v logit / T - log(max(-log u, 1e-10)) and
     its global index, u from Philox4x32-10 keyed by `seed` at counter (global
-    index / 4, row, step).  temperatures [B] f32 (<= 0: greedy).  Returns
+    index / 4, row, step [+ step_device, an int64 [1] cuda tensor read by the
+    kernel, so a graph replay can advance it]).  temperatures [B] f32 (<= 0:
+    greedy).  Returns
     (value [B] f32, index [B] int64); over shards, the largest value (ties to
     the lowest index) is the row's token."""
     _need(logits.dim() == 2 and logits.is_cuda and logits.stride(1) == 1, "logits: [B, V] rows")
@@ -277,9 +279,11 @@ def sample(logits: torch.Tensor, temperatures: torch.Tensor, seed: int, step: in
         out_value = torch.empty(B, dtype=torch.float32, device=logits.device)
     if out_index is None:
         out_index = torch.empty(B, dtype=torch.int64, device=logits.device)
+    if step_device is not None:
+        _need(step_device.dtype == torch.int64 and step_device.is_cuda, "step_device: int64")
     check(lib.nvkv_sample(_ptr(logits), B, V, logits.stride(0), int(vocab_offset),
                           _ptr(temperatures), int(seed) & (2**64 - 1), int(step) & (2**64 - 1),
-                          _ptr(out_value), _ptr(out_index), dt, _stream()))
+                          _ptr(step_device), _ptr(out_value), _ptr(out_index), dt, _stream()))
     return out_value, out_index
 
 

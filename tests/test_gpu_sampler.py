@@ -14,7 +14,8 @@ distribution the reference samples from.
 * The Qwen3 driver's sample() equals nvkv_sample over its own logits, and is
   greedy at T = 0.
 * The serving loop with per-request temperatures is reproducible for a seed,
-  and its T = 0 requests match the greedy completions.
+  with or without CUDA-graph replay of its decode steps, and its T = 0
+  requests match the greedy completions.
 """
 import numpy as np
 import pytest
@@ -140,15 +141,18 @@ def test_engine_sampling_is_reproducible():
     rng = np.random.default_rng(4)
     prompts = [rng.integers(0, G.CFG.vocab_size, int(L)).tolist() for L in (40, 97, 130, 64)]
 
-    def run(temps, seed):
+    def run(temps, seed, graphs=True):
         model.allocate_kv_cache(12, G.P)
-        eng = Engine(model, 12, G.P, max_num_batched_tokens=1024, max_model_len=4096, seed=seed)
+        eng = Engine(model, 12, G.P, max_num_batched_tokens=1024, max_model_len=4096, seed=seed,
+                     cuda_graphs=graphs)
         out = eng.generate(prompts, 10, temperature=temps)
+        assert (eng.graph_steps > 0) == graphs  # decode steps replayed a captured graph
         eng.close()
         return out
 
     a = run([1.0, 0.8, 1.2, 0.5], 1)
     assert a == run([1.0, 0.8, 1.2, 0.5], 1)
+    assert a == run([1.0, 0.8, 1.2, 0.5], 1, graphs=False)  # graph replays draw the eager noise
     assert a != run([1.0, 0.8, 1.2, 0.5], 2)
     mixed = run([0.0, 0.8, 0.0, 0.5], 1)
     greedy = run(0.0, 1)

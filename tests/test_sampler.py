@@ -69,9 +69,12 @@ def test_zero_temperature_is_greedy():
 def test_sample_abi_validation_host_only():
     from nvkv._lib import lib, ERR_INVALID_ARG, ERR_UNSUPPORTED, OK, DTYPE_BF16
     p = ctypes.c_void_p(16)
-    assert lib.nvkv_sample(None, 0, 10, 10, 0, None, 1, 1, None, None, DTYPE_BF16, None) == OK
-    assert lib.nvkv_sample(None, 4, 10, 10, 0, p, 1, 1, p, p, DTYPE_BF16, None) == ERR_INVALID_ARG
-    assert lib.nvkv_sample(p, 4, 10, 8, 0, p, 1, 1, p, p, DTYPE_BF16, None) == ERR_INVALID_ARG
-    assert lib.nvkv_sample(p, 4, 0, 8, 0, p, 1, 1, p, p, DTYPE_BF16, None) == ERR_INVALID_ARG
-    assert lib.nvkv_sample(p, 4, 10, 10, 0, p, 1, 1, p, p, 7, None) == ERR_UNSUPPORTED
-    assert lib.nvkv_sample(p, 4, 10, 10, 2**34, p, 1, 1, p, p, DTYPE_BF16, None) == ERR_UNSUPPORTED
+    n = None
+    assert lib.nvkv_sample(None, 0, 10, 10, 0, None, 1, 1, n, None, None, DTYPE_BF16, None) == OK
+    assert lib.nvkv_sample(None, 4, 10, 10, 0, p, 1, 1, n, p, p, DTYPE_BF16,
+                           None) == ERR_INVALID_ARG
+    assert lib.nvkv_sample(p, 4, 10, 8, 0, p, 1, 1, n, p, p, DTYPE_BF16, None) == ERR_INVALID_ARG
+    assert lib.nvkv_sample(p, 4, 0, 8, 0, p, 1, 1, n, p, p, DTYPE_BF16, None) == ERR_INVALID_ARG
+    assert lib.nvkv_sample(p, 4, 10, 10, 0, p, 1, 1, n, p, p, 7, None) == ERR_UNSUPPORTED
+    assert lib.nvkv_sample(p, 4, 10, 10, 2**34, p, 1, 1, n, p, p, DTYPE_BF16,
+                           None) == ERR_UNSUPPORTED
