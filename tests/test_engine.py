@@ -52,6 +52,9 @@ class _FakeModel:
         # the metadata must be self-consistent: slots follow the block tables
         bt = st.block_tables.numpy()
         cu_q, cu_k = st.cu_seqlens_q.numpy(), st.cu_seqlens_k.numpy()
+        # the fp8 pool's dequantisation workspace: the prompts' keys exactly
+        ql, kl = np.diff(cu_q.astype(np.int64)), np.diff(cu_k.astype(np.int64))
+        assert st.prompt_kv_tokens == (int(kl[ql > 1].sum()) if st.max_seqlen_q > 1 else 0)
         for b in range(len(cu_q) - 1):
             q0, q1 = int(cu_q[b]), int(cu_q[b + 1])
             k_len = int(cu_k[b + 1] - cu_k[b])
