@@ -4,7 +4,7 @@ hot path, tensor-parallel over N GPUs (one process per GPU).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nvkv|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Workload (Qwen3-8B shapes, random-init weights): 256
+Workload (benchmark config 4, Qwen3-8B shapes, random-init weights): 256
 running sequences whose 1024-token prompts are already prefilled and which are
 mid-generation, so their contexts are drawn (seeded) uniform in [1025, 1536];
 one step decodes one token for every sequence through all 36 layers:
@@ -470,7 +470,7 @@ def run_workload(model, world, dev, prompts, max_tokens, num_blocks, warm_prompt
 
 
 def workload_config4(model, world, dev, kv_fp8=False):
-    """BASELINE config 4 end to end: 256 requests x 1024-token prompts of
+    """benchmark config 4 end to end: 256 requests x 1024-token prompts of
     uniform random ids, 512 greedy tokens each, P=256, every step through the
     engine loop (prefill and mixed steps at the 16384-token budget, then
     decode); kv_fp8 runs it over the optional fp8 (e4m3) pool."""
@@ -487,7 +487,7 @@ def workload_config4(model, world, dev, kv_fp8=False):
 
 
 def workload_config3(world, rank, dev, comm):
-    """Qwen3-4B (random-init bf16), 128 requests with
+    """benchmark config 3: Qwen3-4B (random-init bf16), 128 requests with
     prompts U[128, 2048] of uniform random ids, 256 greedy tokens each,
     continuous batching with mixed prefill/decode steps."""
     import torch
@@ -510,7 +510,7 @@ def workload_config3(world, rank, dev, comm):
 
 
 def workload_config1(dev, cpu=True):
-    """BASELINE config 1's workload: Qwen3-0.6B architecture (random-init),
+    """benchmark config 1's workload: Qwen3-0.6B architecture (random-init),
     4 sequences with prompts U[64, 256] of uniform random ids, 32 greedy
     tokens each, P=256.  GPU: the nvkv path in bf16 through the engine loop
     (host clock, end to end).  CPU (`cpu_baseline`): the reference's fp32
@@ -559,7 +559,7 @@ def workload_config1(dev, cpu=True):
 
 
 def workload_config5(world, rank, dev, comm, steps=128):
-    """BASELINE config 5 at TP8: Qwen3-32B (random-init bf16), 64 sequences
+    """benchmark config 5 at TP8: Qwen3-32B (random-init bf16), 64 sequences
     whose 32768-token contexts are already in the KV cache (filled with
     random values instead of a 2M-token prefill), then `steps` greedy decode
     tokens each.  One decode step (device-side metadata via
@@ -1074,7 +1074,7 @@ def cpu_reference(steps=3, warmup=1, num_seqs=CPU_SAMPLE_SEQS):
 
 
 def op_level_config2(seed=2, reps=20):
-    """BASELINE config 2 at operator level: paged decode attention, B=64 decode
+    """benchmark config 2 at operator level: paged decode attention, B=64 decode
     queries, 16 q / 8 kv heads, L ~ U[512, 4096], P=256, block tables a seeded
     permutation of a 2048-block pool, q/k/v ~ N(0,1).  Reports the nvkv kernel
     (CUDA graph of `reps` calls, CUDA events), the installed flash_attn 2.8.3
@@ -1135,7 +1135,7 @@ def op_level_config2(seed=2, reps=20):
     nbytes = int(lens.sum()) * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * int(need.sum())
     nv_us = graph_us(nv)
     peak, _ = load_peak()
-    res = {"workload": "BASELINE config 2: paged decode attention, B=64, 16q/8kv, D=128, "
+    res = {"workload": "benchmark config 2: paged decode attention, B=64, 16q/8kv, D=128, "
                        "L~U[512,4096], P=256, 2048-block pool, bf16",
            "nvkv_us": round(nv_us, 2),
            "nvkv_gbs": round(nbytes / (nv_us * 1e-6) / 1e9, 1),

@@ -3,7 +3,7 @@
     python kbench.py [--case NAME ...] [--iters N]
 
 Cases (one JSON line each; bytes/flops are the algorithmic figures):
-  store_cfg2      nvkv_store_kvcache: 64 tokens + 8 padded
+  store_cfg2      nvkv_store_kvcache, benchmark config 2: 64 tokens + 8 padded
                   slots, 8 kv heads, 2048-block pool                     (HBM)
   store_prefill   the same at T = 16384 (a full 16384-token prefill step)  (HBM)
   prologue_8b     nvkv_qknorm_rope + fused store, Qwen3-8B TP1 decode T=256 (HBM)
@@ -236,7 +236,7 @@ def case_prefill(iters, nseq=16, L=1024, hq=32, hkv=8):
 
 
 def case_mixed(iters, tp=1):
-    """BASELINE config 3 (Qwen3-4B, 32q/8kv, TP1/2): one continuous-batching
+    """benchmark config 3 (Qwen3-4B, 32q/8kv, TP1/2): one continuous-batching
     step of 120 decoding sequences (contexts U[129, 2304]) and 8 fresh
     prompts U[128, 2048] in one nvkv_paged_attention call (decode kernel +
     tcgen05 kernel), and each part alone for the split."""

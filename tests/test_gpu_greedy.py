@@ -1,4 +1,4 @@
-"""Greedy-stream parity gate (BASELINE config 1 shape): Qwen3-0.6B
+"""Greedy-stream parity gate (benchmark config 1 shape): Qwen3-0.6B
 architecture, seeded random-init weights, sequences with prompt lengths
 U[64, 256] and uniform token ids, 32 greedy tokens each, KV block size 256.
 

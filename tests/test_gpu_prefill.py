@@ -98,7 +98,7 @@ def test_prefill_page_128():
 
 @pytest.mark.parametrize("tp", [1, 2])
 def test_config3_mixed_step_qwen3_4b(tp):
-    """BASELINE config 3 (Qwen3-4B, 32 q / 8 kv heads, TP1/2): a continuous-
+    """benchmark config 3 (Qwen3-4B, 32 q / 8 kv heads, TP1/2): a continuous-
     batching step with decoding sequences (contexts U[129, 2304]) next to
     fresh prompts and a prefix-cache-hit chunk, at the per-rank head counts."""
     rng = np.random.default_rng(30 + tp)
