@@ -42,6 +42,32 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(
   const int lane = tid & 31, warp = tid >> 5;
 
   const int64_t pos = positions[t];
+  // the warp's first kPre rows are loaded before the RoPE table is built, so
+  // their latency overlaps the trigonometry and the barrier (8B TP1 layer,
+  // 256 tokens: 5.29 -> 5.03 us)
+  constexpr int kPre = 12;
+  const int i0 = 2 * lane;  // this lane's two rotation pairs: i0, i0+1
+  const int rows = num_q_heads + 2 * num_kv_heads;
+  const T* src_tok = qkv + t * qkv_stride;
+  uint32_t pa[kPre], pb[kPre];
+#pragma unroll
+  for (int k = 0; k < kPre; ++k) {
+    const int r = warp + 8 * k;
+    if (r < rows) {
+      pa[k] = *reinterpret_cast<const uint32_t*>(src_tok + (int64_t)r * kRopeD + i0);
+      pb[k] = *reinterpret_cast<const uint32_t*>(src_tok + (int64_t)r * kRopeD + 64 + i0);
+    }
+  }
+  const bool do_norm = (q_w != nullptr);
+  float wq[4], wk[4];
+  if (do_norm) {
+    float2 a = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(q_w + i0));
+    float2 b = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(q_w + 64 + i0));
+    wq[0] = a.x; wq[1] = a.y; wq[2] = b.x; wq[3] = b.y;
+    a = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(k_w + i0));
+    b = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(k_w + 64 + i0));
+    wk[0] = a.x; wk[1] = a.y; wk[2] = b.x; wk[3] = b.y;
+  }
   if (tid < kRopeD / 2) {
     if (tid == 0 && (pos < 0 || pos >= max_position)) record_error(err, NVKV_DEVERR_POSITION_RANGE);
     // rotary_embedding.rs:31-49 in f32, then the cast of :60
@@ -61,27 +87,10 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(
   }
   __syncthreads();
 
-  const int i0 = 2 * lane;  // this lane's two rotation pairs: i0, i0+1
   const float c0 = s_cos[i0], c1 = s_cos[i0 + 1];
   const float sn0 = s_sin[i0], sn1 = s_sin[i0 + 1];
-  const bool do_norm = (q_w != nullptr);
-  float wq[4], wk[4];
-  if (do_norm) {
-    float2 a = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(q_w + i0));
-    float2 b = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(q_w + 64 + i0));
-    wq[0] = a.x; wq[1] = a.y; wq[2] = b.x; wq[3] = b.y;
-    a = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(k_w + i0));
-    b = DT<T>::to_f2(*reinterpret_cast<const uint32_t*>(k_w + 64 + i0));
-    wk[0] = a.x; wk[1] = a.y; wk[2] = b.x; wk[3] = b.y;
-  }
-
-  const int rows = num_q_heads + 2 * num_kv_heads;
-  const T* src_tok = qkv + t * qkv_stride;
   const int64_t kv_row = (int64_t)num_kv_heads * kRopeD;
-  for (int r = warp; r < rows; r += 8) {
-    const T* src = src_tok + (int64_t)r * kRopeD;
-    const uint32_t ua = *reinterpret_cast<const uint32_t*>(src + i0);
-    const uint32_t ub = *reinterpret_cast<const uint32_t*>(src + 64 + i0);
+  auto row_out = [&](int r, uint32_t ua, uint32_t ub) {
     if (r >= num_q_heads + num_kv_heads) {  // V head: plain copy
       const int h = r - num_q_heads - num_kv_heads;
       if (v_out) {
@@ -94,7 +103,7 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(
         *reinterpret_cast<uint32_t*>(d + i0) = ua;
         *reinterpret_cast<uint32_t*>(d + 64 + i0) = ub;
       }
-      continue;
+      return;
     }
     const bool is_q = r < num_q_heads;
     const float2 fa = DT<T>::to_f2(ua), fb = DT<T>::to_f2(ub);
@@ -136,8 +145,19 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(
         *reinterpret_cast<uint32_t*>(d + 64 + i0) = ob;
       }
     }
+  };
+#pragma unroll
+  for (int k = 0; k < kPre; ++k) {
+    const int r = warp + 8 * k;
+    if (r < rows) row_out(r, pa[k], pb[k]);
+  }
+  for (int r = warp + 8 * kPre; r < rows; r += 8) {  // rows beyond the preloaded ones
+    const T* src = src_tok + (int64_t)r * kRopeD;
+    row_out(r, *reinterpret_cast<const uint32_t*>(src + i0),
+            *reinterpret_cast<const uint32_t*>(src + 64 + i0));
   }
 }
+
 
 }  // namespace nvkv
 
