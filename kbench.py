@@ -454,6 +454,10 @@ CASES = {
         "decode_32b_tp8_fp8", np.full(64, 32768), 8, 1, 64 * 128 + 2, it, 2),
     "sample_8b_tp1": lambda it: case_sample("sample_8b_tp1", 256, 151936, it),
     "sample_8b_tp8": lambda it: case_sample("sample_8b_tp8", 256, 151936 // 8, it),
+    "decode_g16": lambda it: case_decode(
+        "decode_g16", np.random.default_rng(8).integers(2048, 4097, 64), 16, 1, 1100, it, 8),
+    "decode_g16_fp8": lambda it: case_decode_fp8(
+        "decode_g16_fp8", np.random.default_rng(8).integers(2048, 4097, 64), 16, 1, 1100, it, 8),
     "prefill_8b": lambda it: case_prefill(it),
     "step_metadata": lambda it: case_step_metadata(256, it),
     "mixed_4b_tp1": lambda it: case_mixed(it, 1),
