@@ -188,14 +188,17 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
  * NVKV_DEVERR_SLOT_RANGE).  Bit-exact with the formula above.
  *
  * nvkv_paged_attention_fp8: nvkv_paged_attention over an fp8 pool (paged
- * only: block_tables required; page_size a multiple of 128).  q/out are
- * bf16/f16 as `dtype`.  Decode rows read the codes directly (half the bytes);
+ * only: block_tables required; page_size a multiple of 128; caches, scale
+ * arrays, q, out and workspace 16-byte aligned).  q/out are bf16/f16 as
+ * `dtype`.  Decode rows read the codes directly (half the bytes);
  * prompt rows (q_len > 1) are dequantised into the workspace first, so the
  * caller passes prompt_kv_tokens >= the sum of k_len over the batch's
  * q_len > 1 sequences (0 when max_seqlen_q <= 1); a prompt that does not fit
  * is skipped and reported as NVKV_DEVERR_SEQLEN.  The workspace holds
  * nvkv_paged_attention_fp8_workspace_size() bytes.  Outputs are the attention
- * of q over the dequantised keys and values (values rounded to the dtype).
+ * of q over the dequantised keys and values: decode rows take S = (q . codes)
+ * x k_scale and P x v_scale in f32 (q split exactly into e4m3 pieces for the
+ * products), prompt rows attend over values rounded to the dtype.
  * ---------------------------------------------------------------------- */
 int nvkv_store_kvcache_fp8(const void* key, const void* value, void* k_cache, void* v_cache,
                            float* k_scale, float* v_scale, const int64_t* slot_mapping,
