@@ -197,8 +197,9 @@ int nvkv_paged_attention(const void* q, int64_t q_stride, int64_t num_q_tokens,
  * is skipped and reported as NVKV_DEVERR_SEQLEN.  The workspace holds
  * nvkv_paged_attention_fp8_workspace_size() bytes.  Outputs are the attention
  * of q over the dequantised keys and values: decode rows take S = (q . codes)
- * x k_scale and P x v_scale in f32 (q split exactly into e4m3 pieces for the
- * products), prompt rows attend over values rounded to the dtype.
+ * x k_scale and P x v_scale in f32 (q enters the products as e4m3 pieces
+ * that hold it exactly down to 2^-10 of the group's largest |q|), prompt
+ * rows attend over values rounded to the dtype.
  * ---------------------------------------------------------------------- */
 int nvkv_store_kvcache_fp8(const void* key, const void* value, void* k_cache, void* v_cache,
                            float* k_scale, float* v_scale, const int64_t* slot_mapping,
