@@ -184,3 +184,16 @@ def test_decode_plan_one_wave_rule():
     assert ws(236, 4, 1, 1536) > 0       # below: split to fill the machine
     assert ws(64, 16, 8, 4096) > 0       # config 2: 64-tile contexts split
     assert ws(64, 8, 1, 32768) > 0       # 32B TP8 long context
+
+
+def test_fp8_workspace_follows_its_plan():
+    """The fp8 pool's decode plan (128-key tiles) seen through its workspace
+    query: one wave of unsplit CTAs needs no scratch, a batch that splits
+    does, and prompts add their dequantised rows (K and V, 2 bytes a value)
+    after the decode scratch and the prefill work plan."""
+    from nvkv import ops
+    assert ops.workspace_size_fp8(256, 4, 1, 1, 1536, 0) == 0   # 8B TP8 decode: one wave
+    split = ops.workspace_size_fp8(64, 16, 8, 1, 4096, 0)       # config 2: splits
+    assert split > 0
+    with_prompts = ops.workspace_size_fp8(64, 16, 8, 512, 4096, 4096)
+    assert with_prompts >= split + 4096 * 8 * 128 * 2 * 2
