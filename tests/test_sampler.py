@@ -78,3 +78,18 @@ def test_sample_abi_validation_host_only():
     assert lib.nvkv_sample(p, 4, 10, 10, 0, p, 1, 1, n, p, p, 7, None) == ERR_UNSUPPORTED
     assert lib.nvkv_sample(p, 4, 10, 10, 2**34, p, 1, 1, n, p, p, DTYPE_BF16,
                            None) == ERR_UNSUPPORTED
+
+
+def test_oracle_draws_follow_softmax():
+    """The generator's distribution on the CPU: 49152 draws over eight logits
+    (rows and steps vary the counter) land within 5 standard deviations of
+    softmax(l / T) in every bin."""
+    base = np.array([0.0, 1.0, -1.0, 0.5, 2.0, -3.0, 0.2, 1.5], np.float32)
+    T, B = 0.7, 4096
+    counts = np.zeros(8, np.int64)
+    for step in range(12):
+        _, idx = O.gumbel_sample(np.tile(base, (B, 1)), np.full(B, T, np.float32), 2024, step)
+        counts += np.bincount(idx, minlength=8)
+    n = counts.sum()
+    p = np.exp(base / T) / np.exp(base / T).sum()
+    assert (np.abs(counts - n * p) <= 5 * np.sqrt(n * p * (1 - p)) + 1).all(), (counts, n * p)
